@@ -1,0 +1,565 @@
+#!/usr/bin/env python
+"""Routed-expert MoE layer benchmark on B200.
+
+Workload (the one the metric is quoted on): a
+Qwen3-30B-A3B-shaped MoE layer — hidden 2048, 128 experts, moe_intermediate
+768, top-8 renormalised softmax routing, W4 symmetric group-128 weights with
+bf16 scales — in decode at batch 1.  One *step* is one pass of the hot path
+(router top-k -> permutation -> W4 gate/up + SiLU*up -> W4 down -> weighted
+combine) over one batch of tokens through one layer.  Steps cycle through a
+stack of 48 distinct layers (15 GB of expert weights), so consecutive steps
+never hit the previous layer's weights in the 126 MB L2.
+
+Synthetic data: weights N(0, 0.02) fp32 quantized on the device with the
+reference quantizer's formula; 8 distinct quantized layers are replicated into
+48 separate buffers.  Activations bf16 N(0, 1); router weights bf16
+N(0, 0.02); logits = bf16(x @ Wr^T), one router per layer.
+
+Output: one JSON line (rank 0).  ``value`` is device-timed (CUDA-graph replay
+of the steps with inputs resident in HBM, events on the launching stream,
+max over ranks); ``e2e`` is the same metric through ``MoeLayer.forward`` (the
+public API) with host->device copies of each step's inputs from pinned memory
+and a device->host copy of its output inside the timed region.
+``--impl reference`` times the CPU restatement of the reference's own CPU path
+(nano_ktrans CPUMoEBackend GPTQ branch) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE-layer routed tokens/s and expert-weight HBM GB/s (% peak) at 1/2/4/8 B200"
+CFG = dict(hidden=2048, experts=128, inter=768, top_k=8, bits=4, group=128)
+UNIQUE_LAYERS = 8
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=48 * 2000)
+    ap.add_argument("--warmup", type=int, default=96)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--sweep", default="8,32,64", help="extra decode batch sizes to report ('' = none)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=960)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# peaks, clocks
+# ---------------------------------------------------------------------------
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self._t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic stack
+# ---------------------------------------------------------------------------
+
+
+def make_unique_layer(gen, device):
+    import torch
+
+    from nano_ktrans_b200.weights import LayerWeights, quantize_symmetric
+
+    E, H, I, bits, g = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["bits"], CFG["group"]
+    out = {}
+    for proj, (n, k) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+        q = torch.empty(E, n, k * bits // 8, dtype=torch.uint8, device=device)
+        s = torch.empty(E, n, k // g, dtype=torch.bfloat16, device=device)
+        for e0 in range(0, E, 16):
+            w = torch.randn(16 * n, k, generator=gen, device=device) * 0.02
+            qw = quantize_symmetric(w, group_size=g, bits=bits)
+            q[e0:e0 + 16] = qw.qweight.view(torch.uint8).view(16, n, -1)
+            s[e0:e0 + 16] = qw.scales.view(16, n, -1).to(torch.bfloat16)
+            del w, qw
+        out[proj] = (q, s)
+    return LayerWeights(bits=bits, group_size=g, gate_q=out["gate"][0], gate_s=out["gate"][1],
+                        up_q=out["up"][0], up_s=out["up"][1], down_q=out["down"][0], down_s=out["down"][1])
+
+
+def clone_layer(lw):
+    from nano_ktrans_b200.weights import LayerWeights
+
+    return LayerWeights(bits=lw.bits, group_size=lw.group_size, gate_q=lw.gate_q.clone(), gate_s=lw.gate_s.clone(),
+                        up_q=lw.up_q.clone(), up_s=lw.up_s.clone(), down_q=lw.down_q.clone(), down_s=lw.down_s.clone())
+
+
+def make_inputs(gen, n_layers, batch, device):
+    import torch
+
+    H, E = CFG["hidden"], CFG["experts"]
+    x = torch.randn(n_layers, batch, H, generator=gen, device=device).to(torch.bfloat16)
+    wr = (torch.randn(n_layers, E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    logits = torch.bmm(x, wr.transpose(1, 2))  # bf16 GEMM, as nn.Linear in bf16 computes the router
+    return x, logits.contiguous()
+
+
+def expert_proj_bytes(lw):
+    """Algorithmic bytes of one expert: (gate+up, down) codes + scales."""
+    gu = sum(t[0].numel() * t.element_size() for t in (lw.gate_q, lw.gate_s, lw.up_q, lw.up_s))
+    dn = sum(t[0].numel() * t.element_size() for t in (lw.down_q, lw.down_s))
+    return gu, dn
+
+
+# ---------------------------------------------------------------------------
+# timed device loop
+# ---------------------------------------------------------------------------
+
+
+def run_device(layers, x, logits, outs, steps, warmup, profile_layer_class=None):
+    """Warm up eagerly, capture the L-step cycle in a CUDA graph, replay it to
+    cover `steps` steps.  Returns (ms, per-kernel avg ms or None, launches/step)."""
+    import torch
+
+    L = len(layers)
+    for i in range(warmup):
+        layers[i % L].forward(x[i % L], logits[i % L], out=outs[i % L])
+    torch.cuda.synchronize()
+    launches = layers[0].last_launch_count()
+    full, rem = divmod(steps, L)
+    if profile_layer_class is not None:
+        for lay in layers:
+            lay.profile_begin(profile_layer_class, 1)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g_full = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_full, stream=s):
+        for i in range(L):
+            layers[i].forward(x[i], logits[i], out=outs[i])
+    g_rem = None
+    if rem:
+        g_rem = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_rem, stream=s):
+            for i in range(rem):
+                layers[i].forward(x[i], logits[i], out=outs[i])
+    g_full.replay()  # one untimed replay
+    torch.cuda.synchronize()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(full):
+        g_full.replay()
+    if g_rem is not None:
+        g_rem.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1)
+    kern = None
+    if profile_layer_class is not None:
+        tot, n = 0.0, 0
+        for lay in layers:
+            a, b = lay.profile_end()
+            tot += a
+            n += b
+        kern = tot / max(n, 1)
+    del g_full, g_rem
+    return ms, kern, launches
+
+
+def distinct_experts(layers, logits):
+    import torch
+
+    out = []
+    for lay, lg in zip(layers, logits):
+        ids, _ = lay.route(lg)
+        out.append(int(torch.unique(ids).numel()))
+    return out
+
+
+def run_e2e(layers, x, logits, steps):
+    """Public API with host buffers: H2D inputs, MoeLayer.forward, D2H output."""
+    import torch
+
+    L = len(layers)
+    xh = x.cpu().pin_memory()
+    lh = logits.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xd, ld = torch.empty_like(x), torch.empty_like(logits)
+    od = torch.empty_like(x)
+    for i in range(2 * L):
+        j = i % L
+        xd[j].copy_(xh[j], non_blocking=True)
+        ld[j].copy_(lh[j], non_blocking=True)
+        layers[j].forward(xd[j], ld[j], out=od[j])
+        oh[j].copy_(od[j], non_blocking=True)
+    torch.cuda.synchronize()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        j = i % L
+        xd[j].copy_(xh[j], non_blocking=True)
+        ld[j].copy_(lh[j], non_blocking=True)
+        layers[j].forward(xd[j], ld[j], out=od[j])
+        oh[j].copy_(od[j], non_blocking=True)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    h2d = xh[0].numel() * 2 + lh[0].numel() * 2
+    d2h = oh[0].numel() * 2
+    return ms, h2d, d2h
+
+
+# ---------------------------------------------------------------------------
+# CPU (reference algorithm) timing
+# ---------------------------------------------------------------------------
+
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [p.get("num_threads", 1) for p in threadpool_info() if p.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return 1
+
+
+def host_expert(lw, e):
+    """Copy one expert's codes/scales to the host as oracle QuantLinear triple."""
+    import numpy as np
+    import torch
+
+    from oracle import moe_oracle as mo
+
+    g = lw.group_size if lw.group_size > 0 else None
+    trip = []
+    for q, s in ((lw.gate_q, lw.gate_s), (lw.up_q, lw.up_s), (lw.down_q, lw.down_s)):
+        words = q[e].contiguous().cpu().numpy().view(np.int32)
+        sc = s[e].to(torch.float32).cpu().numpy()
+        k = words.shape[1] * 32 // lw.bits
+        trip.append(mo.QuantLinear(words, sc, g or k, lw.bits))
+    return tuple(trip)
+
+
+def cpu_reference_rate(layer_w, x, logits, seconds: float, max_steps: int):
+    """Run the reference CPU algorithm (oracle port of CPUMoEBackend's GPTQ
+    branch) on whole layer-steps until `seconds` elapse; tokens/s."""
+    import numpy as np
+    import torch
+
+    from oracle import moe_oracle as mo
+
+    L = len(layer_w)
+    T = x.shape[1]
+    xb = x.view(torch.int16).cpu().numpy().view(np.uint16)
+    lb = logits.view(torch.int16).cpu().numpy().view(np.uint16)
+    done, tokens, busy = 0, 0, 0.0
+    cache = {}
+    while done < max_steps and busy < seconds:
+        j = done % L
+        ids, w, _ = mo.route(lb[j], CFG["top_k"], True, True)
+        experts = {}
+        for e in sorted(set(ids.reshape(-1).tolist())):
+            key = (id(layer_w[j]), e)
+            if key not in cache:
+                cache[key] = host_expert(layer_w[j], e)
+            experts[e] = cache[key]
+        t0 = time.perf_counter()
+        mo.offload_forward(xb[j], ids, w, _Dense(experts, CFG["experts"]))
+        busy += time.perf_counter() - t0
+        done += 1
+        tokens += T
+    return tokens / busy, done, busy
+
+
+class _Dense(dict):
+    """Expert table with len() == num_experts for the oracle's expert scan."""
+
+    def __init__(self, d, n):
+        super().__init__(d)
+        self.n = n
+
+    def __len__(self):
+        return self.n
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(v: float) -> float:
+    import torch
+
+    if not torch.distributed.is_initialized():
+        return v
+    t = torch.tensor([v], device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def config_block(args, world):
+    return {"workload": "qwen3-30b-a3b moe layer decode (BASELINE config 2)", "hidden": CFG["hidden"],
+            "experts": CFG["experts"], "moe_intermediate": CFG["inter"], "top_k": CFG["top_k"],
+            "routing": "softmax top-k renormalised", "weights": "W4 symmetric group-128, bf16 scales",
+            "batch_tokens": args.batch, "layers_cycled": args.layers, "unique_layer_contents": UNIQUE_LAYERS,
+            "l2": "inputs larger than L2: steps cycle 48 distinct layer buffers (15 GB)",
+            "parallelism": f"replicas x{world} (decode does not shard)"}
+
+
+def main_reference(args):
+    """CPU restatement of the reference path on the host cores."""
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.manual_seed(args.seed)
+    gen = torch.Generator().manual_seed(args.seed)
+    from nano_ktrans_b200.weights import quantize_symmetric
+
+    # one layer of 128 experts generated on the CPU (torch) with the same formula
+    E, H, I = CFG["experts"], CFG["hidden"], CFG["inter"]
+    from oracle import moe_oracle as mo
+
+    experts = {}
+    for e in range(E):
+        trip = []
+        for n, k in ((I, H), (I, H), (H, I)):
+            q = quantize_symmetric(torch.randn(n, k, generator=gen) * 0.02, group_size=CFG["group"])
+            trip.append(mo.QuantLinear(q.qweight.numpy(), q.scales.numpy(), CFG["group"], 4))
+        experts[e] = tuple(trip)
+    n_in = 16
+    x = torch.randn(n_in, args.batch, H, generator=gen).to(torch.bfloat16)
+    wr = (torch.randn(E, H, generator=gen) * 0.02).to(torch.bfloat16)
+    logits = (x.float() @ wr.float().T).to(torch.bfloat16)
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    lb = logits.view(torch.int16).numpy().view(np.uint16)
+    table = _Dense(experts, E)
+    for i in range(min(args.warmup, 2)):
+        ids, w, _ = mo.route(lb[i % n_in], CFG["top_k"], True, True)
+        mo.offload_forward(xb[i % n_in], ids, w, table)
+    done, busy = 0, 0.0
+    while done < args.steps and busy < 60.0:
+        ids, w, _ = mo.route(lb[done % n_in], CFG["top_k"], True, True)
+        t0 = time.perf_counter()
+        mo.offload_forward(xb[done % n_in], ids, w, table)
+        busy += time.perf_counter() - t0
+        done += 1
+    v = done * args.batch / busy
+    cores = blas_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "steps_run": done, "warmup": args.warmup, "ms_per_step": 1000 * busy / done,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(args, 1),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{done} whole layer-steps of the workload (bounded at 60 s of CPU time); "
+                                   "oracle port of CPUMoEBackend GPTQ grouped W4A32 path"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return main_reference(args)
+    import torch
+
+    from nano_ktrans_b200 import _lib
+    from nano_ktrans_b200.moe_layer import MoeLayer
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 1000 * rank)
+    uniq = [make_unique_layer(gen, dev) for _ in range(min(UNIQUE_LAYERS, args.layers))]
+    lws = [uniq[i] if i < len(uniq) else clone_layer(uniq[i % len(uniq)]) for i in range(args.layers)]
+    max_b = max([args.batch] + [int(b) for b in args.sweep.split(",") if b])
+    layers = [MoeLayer(lw, top_k=CFG["top_k"], router_use_softmax=True, normalize_topk_prob=True, max_tokens=max_b)
+              for lw in lws]
+    x, logits = make_inputs(gen, args.layers, args.batch, dev)
+    outs = torch.empty_like(x)
+    gu_bytes, dn_bytes = expert_proj_bytes(lws[0])
+    peak, peak_kind = hbm_peak()
+
+    distinct = distinct_experts(layers, logits)
+    L = args.layers
+    steps_bytes = [distinct[i % L] * (gu_bytes + dn_bytes) for i in range(args.steps)]
+
+    with ClockSampler(local) as clk:
+        ms, k_ms, launches = run_device(layers, x, logits, outs, args.steps, args.warmup,
+                                        profile_layer_class=_lib.K_GATEUP)
+    ms = max_over_ranks(ms)
+    tokens = args.steps * args.batch * world
+    value = tokens / (ms / 1e3)
+    alg_bytes = sum(steps_bytes)
+    gbs = alg_bytes * world / (ms / 1e3) / 1e9
+    # roofline of the dominant kernel (gate/up): its algorithmic bytes per launch / its event time
+    gu_per_launch = statistics.mean(d * gu_bytes for d in distinct)
+    achieved = gu_per_launch / (k_ms / 1e3) / 1e9
+    traffic = read_traffic("gateup", args.batch)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u4 codes, f32 accumulate, bf16 io", "data": "synthetic",
+        "config": config_block(args, world),
+        "expert_weight_gbs": gbs, "expert_weight_frac_of_peak": gbs / world / peak,
+        "roofline": {"bound": "hbm", "kernel": "expert_matvec_kernel<4,32,gate/up>", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": gu_per_launch,
+                     "avg_launch_ms": k_ms},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+    }
+
+    if not args.no_e2e:
+        e_ms, h2d, d2h = run_e2e(layers, x, logits, args.e2e_steps)
+        e_ms = max_over_ranks(e_ms)
+        line["e2e"] = {"value": args.e2e_steps * args.batch * world / (e_ms / 1e3), "unit": "tokens/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
+                       "api": "MoeLayer.forward per step, eager (pinned host buffers)"}
+
+    sweep = {}
+    for b in [int(b) for b in args.sweep.split(",") if b]:
+        xb_, lb_ = make_inputs(gen, args.layers, b, dev)
+        ob_ = torch.empty_like(xb_)
+        d_b = distinct_experts(layers, lb_)
+        st = 48 * 100
+        s_ms, s_k, _ = run_device(layers, xb_, lb_, ob_, st, 48, profile_layer_class=_lib.K_GATEUP)
+        s_ms = max_over_ranks(s_ms)
+        byt = sum(d_b[i % L] * (gu_bytes + dn_bytes) for i in range(st))
+        sweep[str(b)] = {"tokens_per_s": st * b * world / (s_ms / 1e3), "ms_per_step": s_ms / st,
+                         "expert_weight_gbs": byt * world / (s_ms / 1e3) / 1e9,
+                         "gateup_kernel_gbs": statistics.mean(d * gu_bytes for d in d_b) / (s_k / 1e3) / 1e9,
+                         "distinct_experts_mean": statistics.mean(d_b)}
+    if sweep:
+        line["sweep"] = sweep
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, n, busy = cpu_reference_rate(lws, x, logits, args.cpu_seconds, 10 ** 6)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+                                "sample": f"{n} layer-steps at batch {args.batch} ({busy:.1f} s), oracle port of "
+                                          "CPUMoEBackend GPTQ grouped W4A32 path on the same weights"}
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if torch.distributed.is_initialized():
+        torch.distributed.destroy_process_group()
+
+
+def read_traffic(kernel: str, batch: int):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/ncu_traffic.txt):
+    lines `<kernel> <batch> <bytes_per_launch>`."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        with open(p) as f:
+            for ln in f:
+                parts = ln.split()
+                if len(parts) >= 3 and not ln.startswith("#") and parts[0] == kernel and int(parts[1]) == batch:
+                    return float(parts[2])
+    except OSError:
+        pass
+    return None
+
+
+if __name__ == "__main__":
+    main()

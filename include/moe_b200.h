@@ -1,0 +1,173 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) routed-expert MoE path.
+ *
+ * This library is the device backend for nano-ktrans's HybridMoE routed
+ * experts.  Each entry point replaces one step of the reference's Python
+ * path (paths are relative to the nano-ktrans project root):
+ *
+ *   moe_route            nano_ktrans/layers/hybrid_moe.py:3321-3329
+ *                        (softmax -> top-k -> renormalise, or Mixtral's
+ *                         top-k -> softmax)
+ *   moe_experts_forward  nano_ktrans/kernels/offload_backend.py:40-52
+ *                        ExpertOffloadBackend.submit_forward, as implemented
+ *                        by CPUMoEBackend's GPTQ branch
+ *                        nano_ktrans/kernels/cpu_moe.py:491-539 (per-expert
+ *                        grouped W4A32 matvec quantized_ops.py:86-124,
+ *                        SiLU(gate)*up cpu_moe.py:419-450, weighted
+ *                        index_add_ combine cpu_moe.py:528-538)
+ *   moe_forward          HybridMoE.forward with every expert offloaded
+ *                        (hybrid_moe.py:3310-3570): route + experts
+ *   moe_dequant_rows     GPTQLinearWeight.dequantize
+ *                        nano_ktrans/kernels/weight_loader.py:57-69, for the
+ *                        bit-exact dequantization check
+ *   moe_create / moe_set_weights / moe_last_error / moe_destroy
+ *                        the handle / int-status / caller-error-buffer
+ *                        convention of the reference's native bridge
+ *                        nano_ktrans/kernels/pim_native/host_quantized_bridge.c
+ *                        (pim_quantized_init :233, load_weights :589,
+ *                        set_error :157, shutdown :1306)
+ *
+ * Conventions
+ *   - Every pointer argument named *_dev is device memory on the handle's
+ *     device; nothing in this ABI takes a torch type.
+ *   - Every call that takes a `stream` (a cudaStream_t passed as void*) only
+ *     enqueues work on that stream and returns; results are stream-ordered.
+ *   - Return value 0 = success; otherwise an MOE_E* code, and the message is
+ *     available from moe_last_error().
+ *   - bf16 tensors are passed as raw 16-bit patterns (uint16_t storage).
+ *
+ * Weight layout (device, borrowed by the handle, never copied):
+ *   q[e][n][K*bits/8] uint8  — exactly the little-endian bytes of the
+ *                              reference GPTQLinearWeight.qweight int32 words
+ *                              [N, K*bits/32] (codes LSB-first along K,
+ *                              offset-binary, zero point 2^(bits-1));
+ *   s[e][n][K/group] bf16    — per-group scales.
+ *   gate/up: N = inter, K = hidden.  down: N = hidden, K = inter.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+enum moe_status {
+  MOE_OK = 0,
+  MOE_EINVAL = 1,     /* bad argument or unsupported shape */
+  MOE_ECUDA = 2,      /* a CUDA runtime call failed */
+  MOE_ENOWEIGHTS = 3, /* moe_set_weights was not called */
+  MOE_ERANGE = 4,     /* token count above the handle's max_tokens */
+  MOE_EDEVICE = 5     /* a kernel recorded a bad input (see moe_read_status) */
+};
+
+/* Layer description.  group_size == 0 means one group per output channel
+ * (group = K of each projection). */
+typedef struct moe_layer_desc {
+  int32_t num_experts;
+  int32_t top_k;
+  int32_t hidden_size;
+  int32_t inter_size;
+  int32_t bits;                /* 4 or 8 */
+  int32_t group_size;          /* 0 (per-channel) or a multiple of 32 (W4) / 16 (W8) */
+  int32_t router_use_softmax;  /* 1: Qwen softmax->topk; 0: Mixtral topk->softmax */
+  int32_t normalize_topk_prob; /* renormalise top-k weights (softmax routing only) */
+  int32_t max_tokens;          /* largest T any call will pass */
+  int32_t shared_inter;        /* shared-expert intermediate size, 0 = none */
+} moe_layer_desc;
+
+/* Device pointers to the stacked expert weights (see layout above). */
+typedef struct moe_weights {
+  const void* gate_q_dev;
+  const void* gate_s_dev;
+  const void* up_q_dev;
+  const void* up_s_dev;
+  const void* down_q_dev;
+  const void* down_s_dev;
+  /* shared expert (only read when shared_inter > 0): same per-projection
+   * layout with E = 1, plus the bf16 [hidden] sigmoid-gate vector */
+  const void* shared_gate_q_dev;
+  const void* shared_gate_s_dev;
+  const void* shared_up_q_dev;
+  const void* shared_up_s_dev;
+  const void* shared_down_q_dev;
+  const void* shared_down_s_dev;
+  const void* shared_gate_vec_dev;
+} moe_weights;
+
+int moe_abi_version(void);
+
+/* Create a handle on the current CUDA device; allocates the handle's
+ * workspace (sized by desc->max_tokens). */
+int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_len);
+
+/* Register (borrow) the device weight pointers. */
+int moe_set_weights(void* handle, const moe_weights* w, char* err, size_t err_len);
+
+/* Routing: logits [T, E] bf16 -> topk_ids [T, k] int64, topk_weights [T, k]
+ * bf16.  Ties are broken by (value desc, expert index asc). */
+int moe_route(void* handle, const uint16_t* logits_dev, int32_t num_tokens,
+              int64_t* topk_ids_dev, uint16_t* topk_weights_dev, void* stream);
+
+/* Routed experts + weighted combine:
+ *   out[t] = bf16( sum over slots j, expert e = ids[t][j] ascending, with
+ *                  offload_mask[e] != 0 (or all when the mask is NULL):
+ *                  w[t][j] * down(silu(gate(x[t])) * up(x[t])) )
+ * accumulated in fp32.  When the layer has a shared expert and
+ * `add_shared` is nonzero, sigmoid(x . g_s) * shared(x) is added before the
+ * single bf16 rounding. */
+int moe_experts_forward(void* handle, const uint16_t* x_dev, const int64_t* topk_ids_dev,
+                        const uint16_t* topk_weights_dev, int32_t num_tokens,
+                        const uint8_t* offload_mask_dev, int32_t add_shared,
+                        uint16_t* out_dev, void* stream);
+
+/* moe_route followed by moe_experts_forward (all experts, shared expert
+ * added when present).  topk_ids_dev / topk_weights_dev may be NULL. */
+int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
+                int32_t num_tokens, uint16_t* out_dev, int64_t* topk_ids_dev,
+                uint16_t* topk_weights_dev, void* stream);
+
+/* Dequantize rows [row0, row0+nrows) of projection `proj` (0 gate, 1 up,
+ * 2 down, 3..5 shared gate/up/down) of expert `expert` into fp32 [nrows, K],
+ * with the same unpack code the matvec kernels use. */
+int moe_dequant_rows(void* handle, int32_t proj, int32_t expert, int32_t row0, int32_t nrows,
+                     float* out_dev, void* stream);
+
+/* Copy the device status word to *status (synchronises `stream`).  Nonzero
+ * means a kernel saw an expert id outside [0, E) since the last reset; the
+ * word is cleared by this call. */
+int moe_read_status(void* handle, int32_t* status, void* stream);
+
+/* Kernels launched by the last moe_experts_forward / moe_forward call. */
+int moe_last_launch_count(void* handle);
+
+/* Kernel classes for moe_profile_begin. */
+enum moe_kernel_class {
+  MOE_K_ROUTE = 1,
+  MOE_K_PERMUTE = 2,
+  MOE_K_GATEUP = 3,
+  MOE_K_DOWN = 4,
+  MOE_K_COMBINE = 5
+};
+
+/* Bracket the launch of one kernel class with CUDA events on the launching
+ * stream in each of the next `max_samples` forward calls (no counterpart in
+ * the reference: measurement support, allocates the events). */
+int moe_profile_begin(void* handle, int32_t kernel_class, int32_t max_samples);
+
+/* Wait for the recorded events and return the summed kernel time and the
+ * number of bracketed launches; stops profiling. */
+int moe_profile_end(void* handle, float* total_ms, int32_t* samples);
+
+int moe_last_error(void* handle, char* buf, size_t len);
+void moe_destroy(void* handle);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */

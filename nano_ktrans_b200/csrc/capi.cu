@@ -1,0 +1,396 @@
+// capi.cu — extern "C" entry points declared in include/moe_b200.h.
+//
+// Handle lifecycle and error convention follow the reference's native bridge
+// (nano_ktrans/kernels/pim_native/host_quantized_bridge.c: opaque handle from
+// an init call :233, int status return, caller-provided error buffer filled by
+// set_error :157, explicit shutdown :1306).  Unlike that bridge, every compute
+// entry point only enqueues work on the caller's CUDA stream.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "kernels.h"
+
+namespace {
+
+using moe::QuantProj;
+using moe::RouteTables;
+
+struct Handle {
+  moe_layer_desc d{};
+  int device = 0;
+  int num_sms = 148;
+  moe_weights w{};
+  bool has_weights = false;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  RouteTables rt{};
+  float* hbuf = nullptr;   // [max_pairs][I]
+  float* ybuf = nullptr;   // [max_pairs][H]
+  float* sh_h = nullptr;   // [max_tokens][I_s]
+  float* sh_y = nullptr;   // [max_tokens][H]
+  float* sh_g = nullptr;   // [max_tokens]
+  int64_t* ids_tmp = nullptr;
+  uint16_t* w_tmp = nullptr;
+  std::string err;
+  int last_launches = 0;
+  // profiling: events bracketing one kernel class
+  int prof_class = 0;
+  int prof_max = 0;
+  int prof_n = 0;
+  std::vector<cudaEvent_t> prof_ev;
+};
+
+void prof_mark(Handle* h, int cls, bool after, cudaStream_t st) {
+  if (h->prof_class != cls || h->prof_n >= h->prof_max) return;
+  cudaEventRecord(h->prof_ev[2 * h->prof_n + (after ? 1 : 0)], st);
+  if (after) ++h->prof_n;
+}
+
+void fmt_err(char* buf, size_t len, const char* f, ...) {
+  if (buf == nullptr || len == 0) return;
+  va_list ap;
+  va_start(ap, f);
+  vsnprintf(buf, len, f, ap);
+  va_end(ap);
+}
+
+int fail(Handle* h, int code, const char* f, ...) {
+  char tmp[512];
+  va_list ap;
+  va_start(ap, f);
+  vsnprintf(tmp, sizeof(tmp), f, ap);
+  va_end(ap);
+  if (h) h->err = tmp;
+  return code;
+}
+
+int check_launch(Handle* h, const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(h, MOE_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return MOE_OK;
+}
+
+int proj_group(const moe_layer_desc& d, int k) { return d.group_size > 0 ? d.group_size : k; }
+
+QuantProj make_proj(const Handle* h, const void* q, const void* s, int n, int k) {
+  QuantProj p;
+  p.q = static_cast<const uint8_t*>(q);
+  p.s = static_cast<const uint16_t*>(s);
+  p.n = n;
+  p.k = k;
+  p.group = proj_group(h->d, k);
+  return p;
+}
+
+const char* validate_desc(const moe_layer_desc& d) {
+  if (d.num_experts < 1 || d.num_experts > 1024) return "num_experts must be in [1, 1024]";
+  if (d.top_k < 1 || d.top_k > 16 || d.top_k > d.num_experts) return "top_k must be in [1, min(16, num_experts)]";
+  if (d.bits != 4 && d.bits != 8) return "bits must be 4 or 8";
+  const int align = d.bits == 4 ? 32 : 16;  // codes per 16-byte chunk
+  if (d.hidden_size <= 0 || d.hidden_size % align) return "hidden_size must be a positive multiple of 32 (W4) / 16 (W8)";
+  if (d.inter_size <= 0 || d.inter_size % align) return "inter_size must be a positive multiple of 32 (W4) / 16 (W8)";
+  if (d.shared_inter < 0 || d.shared_inter % align) return "shared_inter must be a multiple of 32 (W4) / 16 (W8)";
+  if (d.group_size < 0) return "group_size must be >= 0";
+  if (d.group_size > 0) {
+    if (d.group_size % align) return "group_size must be a multiple of 32 (W4) / 16 (W8)";
+    if (d.hidden_size % d.group_size || d.inter_size % d.group_size) return "group_size must divide hidden and inter";
+    if (d.shared_inter % d.group_size) return "group_size must divide shared_inter";
+  }
+  if (d.max_tokens < 1) return "max_tokens must be >= 1";
+  return nullptr;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+}  // namespace
+
+extern "C" {
+
+int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_len) {
+  if (desc == nullptr || handle == nullptr) {
+    fmt_err(err, err_len, "moe_create: null argument");
+    return MOE_EINVAL;
+  }
+  if (const char* why = validate_desc(*desc)) {
+    fmt_err(err, err_len, "moe_create: %s", why);
+    return MOE_EINVAL;
+  }
+  Handle* h = new Handle();
+  h->d = *desc;
+  cudaGetDevice(&h->device);
+  cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->device);
+  const moe_layer_desc& d = h->d;
+  const size_t E = d.num_experts, T = d.max_tokens, P = T * d.top_k;
+  const size_t H = d.hidden_size, I = d.inter_size, S = d.shared_inter;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t o_status = take(4), o_counts = take(4 * E), o_offsets = take(4 * (E + 1)), o_active = take(4 * E),
+               o_nact = take(4), o_sorted = take(4 * P), o_pos = take(4 * P), o_h = take(4 * P * I),
+               o_y = take(4 * P * H), o_shh = take(S ? 4 * T * S : 0), o_shy = take(S ? 4 * T * H : 0),
+               o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P);
+  h->ws_bytes = off;
+  cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
+  if (e != cudaSuccess) {
+    fmt_err(err, err_len, "moe_create: cudaMalloc(%zu) failed: %s", h->ws_bytes, cudaGetErrorString(e));
+    delete h;
+    return MOE_ECUDA;
+  }
+  char* b = static_cast<char*>(h->ws);
+  h->rt.status = reinterpret_cast<int32_t*>(b + o_status);
+  h->rt.counts = reinterpret_cast<int32_t*>(b + o_counts);
+  h->rt.offsets = reinterpret_cast<int32_t*>(b + o_offsets);
+  h->rt.active = reinterpret_cast<int32_t*>(b + o_active);
+  h->rt.n_active = reinterpret_cast<int32_t*>(b + o_nact);
+  h->rt.sorted_pair = reinterpret_cast<int32_t*>(b + o_sorted);
+  h->rt.pair_pos = reinterpret_cast<int32_t*>(b + o_pos);
+  h->hbuf = reinterpret_cast<float*>(b + o_h);
+  h->ybuf = reinterpret_cast<float*>(b + o_y);
+  if (S) {
+    h->sh_h = reinterpret_cast<float*>(b + o_shh);
+    h->sh_y = reinterpret_cast<float*>(b + o_shy);
+    h->sh_g = reinterpret_cast<float*>(b + o_shg);
+  }
+  h->ids_tmp = reinterpret_cast<int64_t*>(b + o_ids);
+  h->w_tmp = reinterpret_cast<uint16_t*>(b + o_w);
+  e = cudaMemset(h->ws, 0, h->ws_bytes);
+  if (e != cudaSuccess) {
+    fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
+    cudaFree(h->ws);
+    delete h;
+    return MOE_ECUDA;
+  }
+  *handle = h;
+  return MOE_OK;
+}
+
+int moe_set_weights(void* handle, const moe_weights* w, char* err, size_t err_len) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr || w == nullptr) {
+    fmt_err(err, err_len, "moe_set_weights: null argument");
+    return MOE_EINVAL;
+  }
+  const void* need[] = {w->gate_q_dev, w->gate_s_dev, w->up_q_dev, w->up_s_dev, w->down_q_dev, w->down_s_dev};
+  for (const void* p : need) {
+    if (p == nullptr) {
+      fmt_err(err, err_len, "moe_set_weights: routed-expert weight pointer is NULL");
+      return MOE_EINVAL;
+    }
+    if (reinterpret_cast<uintptr_t>(p) % 16) {
+      fmt_err(err, err_len, "moe_set_weights: weight pointers must be 16-byte aligned");
+      return MOE_EINVAL;
+    }
+  }
+  if (h->d.shared_inter > 0) {
+    const void* sh[] = {w->shared_gate_q_dev, w->shared_gate_s_dev, w->shared_up_q_dev, w->shared_up_s_dev,
+                        w->shared_down_q_dev, w->shared_down_s_dev, w->shared_gate_vec_dev};
+    for (const void* p : sh) {
+      if (p == nullptr) {
+        fmt_err(err, err_len, "moe_set_weights: shared-expert weight pointer is NULL");
+        return MOE_EINVAL;
+      }
+    }
+  }
+  h->w = *w;
+  h->has_weights = true;
+  return MOE_OK;
+}
+
+int moe_route(void* handle, const uint16_t* logits_dev, int32_t T, int64_t* ids_dev, uint16_t* w_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (T < 0) return fail(h, MOE_EINVAL, "moe_route: negative token count");
+  if (T > 0 && (logits_dev == nullptr || ids_dev == nullptr || w_dev == nullptr))
+    return fail(h, MOE_EINVAL, "moe_route: null device pointer");
+  moe::launch_route(logits_dev, T, h->d.num_experts, h->d.top_k, h->d.router_use_softmax != 0,
+                    h->d.normalize_topk_prob != 0, ids_dev, w_dev, static_cast<cudaStream_t>(stream));
+  return check_launch(h, "moe_route");
+}
+
+static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, const uint16_t* wts, int T,
+                           const uint8_t* mask, bool add_shared, uint16_t* out, cudaStream_t st, int launches) {
+  const moe_layer_desc& d = h->d;
+  const int E = d.num_experts, H = d.hidden_size, I = d.inter_size, k = d.top_k;
+  prof_mark(h, MOE_K_PERMUTE, false, st);
+  moe::launch_permute(ids, T, k, E, mask, h->rt, st);
+  prof_mark(h, MOE_K_PERMUTE, true, st);
+  ++launches;
+  const int max_active = std::min(E, T * k);
+  const QuantProj gate = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H);
+  const QuantProj up = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H);
+  const QuantProj down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
+  prof_mark(h, MOE_K_GATEUP, false, st);
+  launches += moe::launch_gateup(d.bits, x, h->rt, k, max_active, 0, gate, up, h->hbuf, h->num_sms, st);
+  prof_mark(h, MOE_K_GATEUP, true, st);
+  prof_mark(h, MOE_K_DOWN, false, st);
+  launches += moe::launch_down(d.bits, h->hbuf, h->rt, max_active, 0, down, h->ybuf, h->num_sms, st);
+  prof_mark(h, MOE_K_DOWN, true, st);
+  const float* sg = nullptr;
+  const float* sy = nullptr;
+  if (add_shared && d.shared_inter > 0) {
+    const int S = d.shared_inter;
+    const QuantProj sgp = make_proj(h, h->w.shared_gate_q_dev, h->w.shared_gate_s_dev, S, H);
+    const QuantProj sup = make_proj(h, h->w.shared_up_q_dev, h->w.shared_up_s_dev, S, H);
+    const QuantProj sdp = make_proj(h, h->w.shared_down_q_dev, h->w.shared_down_s_dev, H, S);
+    moe::launch_shared_gate(x, static_cast<const uint16_t*>(h->w.shared_gate_vec_dev), T, H, h->sh_g, st);
+    ++launches;
+    launches += moe::launch_gateup(d.bits, x, h->rt, 1, 1, T, sgp, sup, h->sh_h, h->num_sms, st);
+    launches += moe::launch_down(d.bits, h->sh_h, h->rt, 1, T, sdp, h->sh_y, h->num_sms, st);
+    sg = h->sh_g;
+    sy = h->sh_y;
+  }
+  prof_mark(h, MOE_K_COMBINE, false, st);
+  moe::launch_combine(ids, wts, h->rt, T, k, H, h->ybuf, sg, sy, out, st);
+  prof_mark(h, MOE_K_COMBINE, true, st);
+  ++launches;
+  h->last_launches = launches;
+  return check_launch(h, "moe_experts_forward");
+}
+
+static int check_forward_args(Handle* h, const void* x, const void* out, int T) {
+  if (!h->has_weights) return fail(h, MOE_ENOWEIGHTS, "weights not set (call moe_set_weights first)");
+  if (T < 0) return fail(h, MOE_EINVAL, "negative token count");
+  if (T > h->d.max_tokens) return fail(h, MOE_ERANGE, "token count %d above max_tokens %d", T, h->d.max_tokens);
+  if (T > 0 && (x == nullptr || out == nullptr)) return fail(h, MOE_EINVAL, "null device pointer");
+  return MOE_OK;
+}
+
+int moe_experts_forward(void* handle, const uint16_t* x_dev, const int64_t* ids_dev, const uint16_t* w_dev, int32_t T,
+                        const uint8_t* mask_dev, int32_t add_shared, uint16_t* out_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (int rc = check_forward_args(h, x_dev, out_dev, T)) return rc;
+  if (T > 0 && (ids_dev == nullptr || w_dev == nullptr)) return fail(h, MOE_EINVAL, "null routing pointer");
+  h->last_launches = 0;
+  if (T == 0) return MOE_OK;
+  return experts_forward(h, x_dev, ids_dev, w_dev, T, mask_dev, add_shared != 0, out_dev,
+                         static_cast<cudaStream_t>(stream), 0);
+}
+
+int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev, int32_t T, uint16_t* out_dev,
+                int64_t* ids_dev, uint16_t* w_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (int rc = check_forward_args(h, x_dev, out_dev, T)) return rc;
+  if (T > 0 && logits_dev == nullptr) return fail(h, MOE_EINVAL, "null logits pointer");
+  h->last_launches = 0;
+  if (T == 0) return MOE_OK;
+  int64_t* ids = ids_dev ? ids_dev : h->ids_tmp;
+  uint16_t* wts = w_dev ? w_dev : h->w_tmp;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  prof_mark(h, MOE_K_ROUTE, false, st);
+  moe::launch_route(logits_dev, T, h->d.num_experts, h->d.top_k, h->d.router_use_softmax != 0,
+                    h->d.normalize_topk_prob != 0, ids, wts, st);
+  prof_mark(h, MOE_K_ROUTE, true, st);
+  return experts_forward(h, x_dev, ids, wts, T, nullptr, true, out_dev, st, 1);
+}
+
+int moe_dequant_rows(void* handle, int32_t proj, int32_t expert, int32_t row0, int32_t nrows, float* out_dev,
+                     void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (!h->has_weights) return fail(h, MOE_ENOWEIGHTS, "weights not set");
+  const moe_layer_desc& d = h->d;
+  const int H = d.hidden_size, I = d.inter_size, S = d.shared_inter;
+  QuantProj p;
+  int E = d.num_experts;
+  switch (proj) {
+    case 0: p = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H); break;
+    case 1: p = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H); break;
+    case 2: p = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I); break;
+    case 3: case 4: case 5:
+      if (S == 0) return fail(h, MOE_EINVAL, "layer has no shared expert");
+      E = 1;
+      p = proj == 3 ? make_proj(h, h->w.shared_gate_q_dev, h->w.shared_gate_s_dev, S, H)
+        : proj == 4 ? make_proj(h, h->w.shared_up_q_dev, h->w.shared_up_s_dev, S, H)
+                    : make_proj(h, h->w.shared_down_q_dev, h->w.shared_down_s_dev, H, S);
+      break;
+    default: return fail(h, MOE_EINVAL, "proj must be 0..5");
+  }
+  if (expert < 0 || expert >= E) return fail(h, MOE_EINVAL, "expert out of range");
+  if (row0 < 0 || nrows < 0 || row0 + nrows > p.n) return fail(h, MOE_EINVAL, "row range out of bounds");
+  if (nrows > 0 && out_dev == nullptr) return fail(h, MOE_EINVAL, "null output");
+  moe::launch_dequant_rows(d.bits, p, expert, row0, nrows, out_dev, static_cast<cudaStream_t>(stream));
+  return check_launch(h, "moe_dequant_rows");
+}
+
+int moe_read_status(void* handle, int32_t* status, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr || status == nullptr) return MOE_EINVAL;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(status, h->rt.status, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(h->rt.status, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return fail(h, MOE_ECUDA, "moe_read_status: %s", cudaGetErrorString(e));
+  return MOE_OK;
+}
+
+int moe_last_launch_count(void* handle) {
+  Handle* h = static_cast<Handle*>(handle);
+  return h ? h->last_launches : 0;
+}
+
+int moe_profile_begin(void* handle, int32_t kernel_class, int32_t max_samples) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (kernel_class < MOE_K_ROUTE || kernel_class > MOE_K_COMBINE || max_samples < 1)
+    return fail(h, MOE_EINVAL, "moe_profile_begin: bad kernel class or sample count");
+  for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
+  h->prof_ev.assign(2 * static_cast<size_t>(max_samples), nullptr);
+  for (auto& e : h->prof_ev) {
+    if (cudaEventCreate(&e) != cudaSuccess) return fail(h, MOE_ECUDA, "moe_profile_begin: cudaEventCreate failed");
+  }
+  h->prof_class = kernel_class;
+  h->prof_max = max_samples;
+  h->prof_n = 0;
+  return MOE_OK;
+}
+
+int moe_profile_end(void* handle, float* total_ms, int32_t* samples) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr || total_ms == nullptr || samples == nullptr) return MOE_EINVAL;
+  double sum = 0.0;
+  for (int i = 0; i < h->prof_n; ++i) {
+    if (cudaEventSynchronize(h->prof_ev[2 * i + 1]) != cudaSuccess) return fail(h, MOE_ECUDA, "event sync failed");
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, h->prof_ev[2 * i], h->prof_ev[2 * i + 1]) != cudaSuccess)
+      return fail(h, MOE_ECUDA, "cudaEventElapsedTime failed");
+    sum += ms;
+  }
+  *total_ms = static_cast<float>(sum);
+  *samples = h->prof_n;
+  h->prof_class = 0;
+  for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
+  h->prof_ev.clear();
+  h->prof_n = h->prof_max = 0;
+  return MOE_OK;
+}
+
+int moe_last_error(void* handle, char* buf, size_t len) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  fmt_err(buf, len, "%s", h->err.c_str());
+  return MOE_OK;
+}
+
+void moe_destroy(void* handle) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return;
+  for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
+  if (h->ws) cudaFree(h->ws);
+  delete h;
+}
+
+}  // extern "C"

@@ -1,0 +1,58 @@
+// kernels.h — host-side launchers for the routed-expert kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+// Routing tables produced by the permute kernel (all device memory).
+struct RouteTables {
+  int32_t* counts;       // [E]     pairs per expert (after the offload mask)
+  int32_t* offsets;      // [E+1]   exclusive prefix of counts
+  int32_t* active;       // [E]     experts with counts > 0, ascending
+  int32_t* n_active;     // [1]
+  int32_t* sorted_pair;  // [P]     pair index p = t*k + j, grouped by expert, p ascending
+  int32_t* pair_pos;     // [P]     position of pair p in sorted_pair, -1 if excluded
+  int32_t* status;       // [1]     error bits (kStatusBadExpertId)
+};
+
+// Expert-projection operand: stacked [E][N][K*bits/8] codes + [E][N][G] scales.
+struct QuantProj {
+  const uint8_t* q;
+  const uint16_t* s;
+  int n;           // output rows
+  int k;           // input dim
+  int group;       // group size along K (== k for per-channel)
+};
+
+void launch_route(const uint16_t* logits, int T, int E, int top_k, bool use_softmax, bool renorm,
+                  int64_t* ids, uint16_t* weights, cudaStream_t st);
+
+void launch_permute(const int64_t* ids, int T, int top_k, int E, const uint8_t* offload_mask,
+                    const RouteTables& rt, cudaStream_t st);
+
+// gate/up projection + SiLU(gate)*up for every (expert, token) pair:
+// h[s][n] for sorted positions s.  When identity_tokens > 0 the routing
+// tables are ignored and a single expert serves tokens 0..identity_tokens-1
+// (the shared expert), h indexed by token.
+int launch_gateup(int bits, const uint16_t* x, const RouteTables& rt, int top_k, int max_active,
+                  int identity_tokens, const QuantProj& gate, const QuantProj& up, float* h,
+                  int num_sms, cudaStream_t st);
+
+// down projection: y[s][n] = down_e(h[s]).
+int launch_down(int bits, const float* h, const RouteTables& rt, int max_active, int identity_tokens,
+                const QuantProj& down, float* y, int num_sms, cudaStream_t st);
+
+// out[t][n] = bf16( sum_{slots by expert asc} w * y[pos] + sg[t] * ys[t][n] )
+void launch_combine(const int64_t* ids, const uint16_t* weights, const RouteTables& rt, int T, int top_k,
+                    int H, const float* y, const float* shared_gate, const float* shared_y, uint16_t* out,
+                    cudaStream_t st);
+
+// sg[t] = sigmoid(x[t] . g) for the shared expert's gate.
+void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t st);
+
+void launch_dequant_rows(int bits, const QuantProj& p, int expert, int row0, int nrows, float* out,
+                         cudaStream_t st);
+
+}  // namespace moe

@@ -1,0 +1,257 @@
+// route.cu — router top-k (K1) and the token -> expert permutation (K1b).
+//
+// K1 follows nano_ktrans/layers/hybrid_moe.py:3321-3329:
+//   softmax routing (Qwen2/Qwen3): p = bf16(softmax_fp32(logits)),
+//     (w, ids) = topk(p, k), and if normalize_topk_prob:
+//     w = bf16(w / bf16(sum(w)))   (bf16 tensor ops: fp32 math, bf16 result)
+//   Mixtral routing: (w, ids) = topk(logits, k); w = bf16(softmax_fp32(w)).
+// One warp per token; each lane holds experts lane, lane+32, ...  Ties are
+// broken by (value desc, expert index asc); NaN ranks above every number, as
+// in torch.topk.
+//
+// K1b replaces the reference's per-expert scan `topk_ids == e` over all E
+// experts (nano_ktrans/kernels/cpu_moe.py:515-527) with one stable counting
+// sort: pairs p = t*k + j are grouped by expert in ascending expert order and,
+// within an expert, in ascending p (so ascending token, the reference's
+// `torch.where(match.any(1))` order).
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moe {
+
+MOE_DEV bool rank_before(float a, int ia, float b, int ib) {
+  const bool na = isnan(a), nb = isnan(b);
+  if (na != nb) return na;
+  if (!na && a != b) return a > b;
+  return ia < ib;
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(256) route_kernel(const uint16_t* __restrict__ logits, int T, int E, int top_k,
+                                                    int use_softmax, int renorm, int64_t* __restrict__ ids,
+                                                    uint16_t* __restrict__ weights) {
+  const int token = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (token >= T) return;
+  const uint16_t* row = logits + static_cast<size_t>(token) * E;
+  float v[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < E ? bf16_to_f32(row[e]) : 0.0f;
+  }
+  if (use_softmax) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i)
+      if (i * 32 + lane < E) m = fmaxf(m, v[i]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      if (i * 32 + lane < E) {
+        v[i] = expf(v[i] - m);
+        s += v[i];
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(kFullMask, s, off);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) v[i] = round_bf16(v[i] / s);
+  }
+
+  // top-k by repeated warp arg-max; lane j keeps the j-th pick
+  uint32_t taken = 0;
+  float my_val = 0.0f;
+  int my_id = 0;
+  for (int j = 0; j < top_k; ++j) {
+    float bv = 0.0f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = i * 32 + lane;
+      if (e < E && !((taken >> i) & 1u) && (bi == 0x7fffffff || rank_before(v[i], e, bv, bi))) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(kFullMask, bv, off);
+      const int oi = __shfl_xor_sync(kFullMask, bi, off);
+      if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ov, oi, bv, bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == j) {
+      my_val = bv;
+      my_id = bi;
+    }
+  }
+
+  float w = my_val;
+  if (use_softmax) {
+    if (renorm) {
+      float s = 0.0f;  // sequential sum in slot order, fp32 (bf16 sum accumulates in fp32)
+      for (int j = 0; j < top_k; ++j) s += __shfl_sync(kFullMask, my_val, j);
+      w = my_val / round_bf16(s);
+    }
+  } else {
+    const float m = __shfl_sync(kFullMask, my_val, 0);
+    const float ex = lane < top_k ? expf(my_val - m) : 0.0f;
+    float s = 0.0f;
+    for (int j = 0; j < top_k; ++j) s += __shfl_sync(kFullMask, ex, j);
+    w = ex / s;
+  }
+  if (lane < top_k) {
+    ids[static_cast<size_t>(token) * top_k + lane] = my_id;
+    weights[static_cast<size_t>(token) * top_k + lane] = f32_to_bf16(w);
+  }
+}
+
+void launch_route(const uint16_t* logits, int T, int E, int top_k, bool use_softmax, bool renorm, int64_t* ids,
+                  uint16_t* weights, cudaStream_t st) {
+  if (T <= 0) return;
+  const dim3 block(256), grid((T + 7) / 8);
+  const int sm = use_softmax ? 1 : 0, rn = renorm ? 1 : 0;
+  if (E <= 32)
+    route_kernel<1><<<grid, block, 0, st>>>(logits, T, E, top_k, sm, rn, ids, weights);
+  else if (E <= 64)
+    route_kernel<2><<<grid, block, 0, st>>>(logits, T, E, top_k, sm, rn, ids, weights);
+  else if (E <= 128)
+    route_kernel<4><<<grid, block, 0, st>>>(logits, T, E, top_k, sm, rn, ids, weights);
+  else if (E <= 256)
+    route_kernel<8><<<grid, block, 0, st>>>(logits, T, E, top_k, sm, rn, ids, weights);
+  else if (E <= 512)
+    route_kernel<16><<<grid, block, 0, st>>>(logits, T, E, top_k, sm, rn, ids, weights);
+  else
+    route_kernel<32><<<grid, block, 0, st>>>(logits, T, E, top_k, sm, rn, ids, weights);
+}
+
+// ---------------------------------------------------------------------------
+// K1b: stable counting sort of (token, slot) pairs by expert.  One CTA of
+// 1024 threads.  Shared memory: cnt[E], run[E], off[E+1], warp_sums[32],
+// wcnt[32][E].
+// ---------------------------------------------------------------------------
+
+__device__ int block_incl_scan(int v, int* warp_sums) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(kFullMask, v, off);
+    if (lane >= off) v += n;
+  }
+  if (lane == 31) warp_sums[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    int w = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int n = __shfl_up_sync(kFullMask, w, off);
+      if (lane >= off) w += n;
+    }
+    warp_sums[lane] = w;
+  }
+  __syncthreads();
+  if (wid > 0) v += warp_sums[wid - 1];
+  __syncthreads();
+  return v;
+}
+
+__global__ void __launch_bounds__(1024) permute_kernel(const int64_t* __restrict__ ids, int P, int E,
+                                                       const uint8_t* __restrict__ mask, RouteTables rt) {
+  extern __shared__ int sm[];
+  int* cnt = sm;                // [E]
+  int* run = cnt + E;           // [E]
+  int* off = run + E;           // [E+1]
+  int* warp_sums = off + E + 1; // [32]
+  int* wcnt = warp_sums + 32;   // [32][E]
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+
+  for (int e = tid; e < E; e += blockDim.x) {
+    cnt[e] = 0;
+    run[e] = 0;
+  }
+  for (int i = tid; i < 32 * E; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+
+  bool bad = false;
+  for (int p = tid; p < P; p += blockDim.x) {
+    const int64_t e = ids[p];
+    if (e < 0 || e >= E) {
+      bad = true;
+      continue;
+    }
+    if (mask == nullptr || mask[e]) atomicAdd(&cnt[e], 1);
+  }
+  if (bad) atomicOr(rt.status, kStatusBadExpertId);
+  __syncthreads();
+
+  // exclusive offsets and the ascending list of active experts (E <= 1024)
+  const int c = tid < E ? cnt[tid] : 0;
+  const int incl = block_incl_scan(c, warp_sums);
+  const int act_incl = block_incl_scan(c > 0 ? 1 : 0, warp_sums);
+  if (tid < E) {
+    off[tid] = incl - c;
+    rt.counts[tid] = c;
+    rt.offsets[tid] = incl - c;
+    if (c > 0) rt.active[act_incl - 1] = tid;
+  }
+  if (tid == E - 1) {
+    off[E] = incl;
+    rt.offsets[E] = incl;
+    *rt.n_active = act_incl;
+  }
+  __syncthreads();
+
+  for (int base = 0; base < P; base += blockDim.x) {
+    const int p = base + tid;
+    int e = -1;
+    if (p < P) {
+      const int64_t e0 = ids[p];
+      if (e0 >= 0 && e0 < E && (mask == nullptr || mask[e0])) e = static_cast<int>(e0);
+    }
+    const uint32_t peers = __match_any_sync(kFullMask, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wcnt[wid * E + e] = __popc(peers);
+    __syncthreads();
+    for (int ee = tid; ee < E; ee += blockDim.x) {
+      int r = run[ee];
+      for (int w = 0; w < 32; ++w) {
+        const int t = wcnt[w * E + ee];
+        wcnt[w * E + ee] = r;
+        r += t;
+      }
+      run[ee] = r;
+    }
+    __syncthreads();
+    if (e >= 0) {
+      const int pos = off[e] + wcnt[wid * E + e] + rank;
+      rt.sorted_pair[pos] = p;
+      rt.pair_pos[p] = pos;
+    } else if (p < P) {
+      rt.pair_pos[p] = -1;
+    }
+    __syncthreads();
+    for (int i = tid; i < 32 * E; i += blockDim.x) wcnt[i] = 0;
+    __syncthreads();
+  }
+}
+
+void launch_permute(const int64_t* ids, int T, int top_k, int E, const uint8_t* offload_mask, const RouteTables& rt,
+                    cudaStream_t st) {
+  const size_t smem = sizeof(int) * (3 * static_cast<size_t>(E) + 1 + 32 + 32 * static_cast<size_t>(E));
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured = true;
+  }
+  permute_kernel<<<1, 1024, smem, st>>>(ids, T * top_k, E, offload_mask, rt);
+}
+
+}  // namespace moe

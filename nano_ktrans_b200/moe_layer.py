@@ -1,0 +1,160 @@
+"""``MoeLayer``: one routed-expert MoE layer bound to ``libmoe_b200.so``.
+
+Thin Python owner of a C-ABI handle (include/moe_b200.h).  Tensors cross the
+boundary as raw device pointers; every call enqueues on a CUDA stream (the
+current torch stream unless one is given) and returns without synchronising.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .weights import LayerWeights
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+class MoeLayer:
+    def __init__(self, weights: LayerWeights, *, top_k: int, router_use_softmax: bool = True,
+                 normalize_topk_prob: bool = True, max_tokens: int = 4096):
+        if not weights.gate_q.is_cuda:
+            raise ValueError("MoeLayer weights must be CUDA tensors (there is no CPU path)")
+        self.weights = weights
+        self.device = weights.gate_q.device
+        self.num_experts = weights.num_experts
+        self.hidden_size = weights.hidden_size
+        self.inter_size = weights.inter_size
+        self.top_k = int(top_k)
+        self.router_use_softmax = bool(router_use_softmax)
+        self.normalize_topk_prob = bool(normalize_topk_prob)
+        self.max_tokens = int(max_tokens)
+        L = _lib.lib()
+        desc = _lib.MoeLayerDesc(self.num_experts, self.top_k, self.hidden_size, self.inter_size, weights.bits,
+                                 weights.group_size, int(self.router_use_softmax), int(self.normalize_topk_prob),
+                                 self.max_tokens, weights.shared_inter)
+        handle = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(1024)
+        with torch.cuda.device(self.device):
+            rc = L.moe_create(ctypes.byref(desc), ctypes.byref(handle), err, len(err))
+        if rc != _lib.MOE_OK:
+            raise _lib.MoeError(rc, err.value.decode())
+        self._h = handle
+        sh = weights.shared or {}
+        w = _lib.MoeWeights(
+            _ptr(weights.gate_q), _ptr(weights.gate_s), _ptr(weights.up_q), _ptr(weights.up_s),
+            _ptr(weights.down_q), _ptr(weights.down_s),
+            _ptr(sh.get("gate_q")), _ptr(sh.get("gate_s")), _ptr(sh.get("up_q")), _ptr(sh.get("up_s")),
+            _ptr(sh.get("down_q")), _ptr(sh.get("down_s")), _ptr(sh.get("gate_vec")))
+        rc = L.moe_set_weights(self._h, ctypes.byref(w), err, len(err))
+        if rc != _lib.MOE_OK:
+            L.moe_destroy(self._h)
+            self._h = None
+            raise _lib.MoeError(rc, err.value.decode())
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.lib().moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------------
+    def _check_tokens(self, x: torch.Tensor) -> int:
+        if x.dim() != 2 or x.shape[1] != self.hidden_size:
+            raise ValueError(f"expected [T, {self.hidden_size}] activations, got {tuple(x.shape)}")
+        if x.dtype != torch.bfloat16 or x.device != self.device:
+            raise ValueError(f"activations must be bf16 on {self.device}")
+        return int(x.shape[0])
+
+    def route(self, router_logits: torch.Tensor, *, out_ids=None, out_weights=None, stream=None):
+        t = int(router_logits.shape[0])
+        if router_logits.dtype != torch.bfloat16 or router_logits.shape[1] != self.num_experts:
+            raise ValueError("router logits must be bf16 [T, E]")
+        logits = router_logits.contiguous()
+        ids = out_ids if out_ids is not None else torch.empty(t, self.top_k, dtype=torch.int64, device=self.device)
+        w = out_weights if out_weights is not None else torch.empty(t, self.top_k, dtype=torch.bfloat16,
+                                                                    device=self.device)
+        _lib.check(_lib.lib().moe_route(self._h, logits.data_ptr(), t, ids.data_ptr(), w.data_ptr(),
+                                        _stream_handle(stream)), self._h, "moe_route")
+        return ids, w
+
+    def experts_forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, *,
+                        offload_mask: Optional[torch.Tensor] = None, add_shared: bool = False, out=None,
+                        stream=None) -> torch.Tensor:
+        t = self._check_tokens(x)
+        ids = topk_ids
+        if ids.dtype != torch.int64:
+            ids = ids.to(torch.int64)
+        w = topk_weights
+        if w.dtype != torch.bfloat16:
+            w = w.to(torch.bfloat16)
+        ids, w, xc = ids.contiguous(), w.contiguous(), x.contiguous()
+        if tuple(ids.shape) != (t, self.top_k) or tuple(w.shape) != (t, self.top_k):
+            raise ValueError(f"routing tensors must be [{t}, {self.top_k}]")
+        mask = None
+        if offload_mask is not None:
+            mask = offload_mask.to(device=self.device, dtype=torch.uint8).contiguous()
+        out = out if out is not None else torch.empty_like(xc)
+        _lib.check(_lib.lib().moe_experts_forward(self._h, xc.data_ptr(), ids.data_ptr(), w.data_ptr(), t,
+                                                  _ptr(mask), int(add_shared), out.data_ptr(),
+                                                  _stream_handle(stream)), self._h, "moe_experts_forward")
+        return out
+
+    def forward(self, x: torch.Tensor, router_logits: torch.Tensor, *, out=None, out_ids=None, out_weights=None,
+                stream=None) -> torch.Tensor:
+        t = self._check_tokens(x)
+        if router_logits.dtype != torch.bfloat16 or tuple(router_logits.shape) != (t, self.num_experts):
+            raise ValueError("router logits must be bf16 [T, E]")
+        xc, lc = x.contiguous(), router_logits.contiguous()
+        out = out if out is not None else torch.empty_like(xc)
+        _lib.check(_lib.lib().moe_forward(self._h, xc.data_ptr(), lc.data_ptr(), t, out.data_ptr(), _ptr(out_ids),
+                                          _ptr(out_weights), _stream_handle(stream)), self._h, "moe_forward")
+        return out
+
+    def dequant_rows(self, proj: int, expert: int, row0: int, nrows: int, stream=None) -> torch.Tensor:
+        k = self.hidden_size if proj in (0, 1, 3, 4) else (self.inter_size if proj == 2 else
+                                                            self.weights.shared_inter)
+        out = torch.empty(nrows, k, dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().moe_dequant_rows(self._h, proj, expert, row0, nrows, out.data_ptr(),
+                                               _stream_handle(stream)), self._h, "moe_dequant_rows")
+        return out
+
+    def read_status(self, stream=None) -> int:
+        st = ctypes.c_int32(0)
+        _lib.check(_lib.lib().moe_read_status(self._h, ctypes.byref(st), _stream_handle(stream)), self._h,
+                   "moe_read_status")
+        return int(st.value)
+
+    def profile_begin(self, kernel_class: int, max_samples: int) -> None:
+        _lib.check(_lib.lib().moe_profile_begin(self._h, kernel_class, max_samples), self._h, "moe_profile_begin")
+
+    def profile_end(self):
+        """(summed kernel ms, number of bracketed launches)"""
+        ms = ctypes.c_float(0.0)
+        n = ctypes.c_int32(0)
+        _lib.check(_lib.lib().moe_profile_end(self._h, ctypes.byref(ms), ctypes.byref(n)), self._h, "moe_profile_end")
+        return float(ms.value), int(n.value)
+
+    def last_launch_count(self) -> int:
+        return int(_lib.lib().moe_last_launch_count(self._h))

@@ -1,0 +1,164 @@
+"""CPU-only tests: the C-ABI library builds, loads and exports every declared
+symbol; argument validation needs no GPU; the host-side container, quantizer,
+device layout and GPTQ loader agree with the oracle."""
+import ctypes
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as mo
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from nano_ktrans_b200 import _lib, build
+
+    build.build()
+    return _lib.lib()
+
+
+def test_library_exports_every_header_symbol(lib):
+    from nano_ktrans_b200 import _lib
+
+    syms = _lib.header_symbols()
+    assert len(syms) >= 10
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in include/moe_b200.h but not exported"
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+    assert lib.moe_abi_version() == 1
+
+
+@pytest.mark.parametrize("field,value,needle", [
+    ("bits", 3, "bits"),
+    ("top_k", 0, "top_k"),
+    ("hidden_size", 100, "hidden_size"),
+    ("group_size", 48, "group_size"),
+    ("num_experts", 2000, "num_experts"),
+    ("max_tokens", 0, "max_tokens"),
+])
+def test_create_rejects_bad_descriptions_without_gpu(lib, field, value, needle):
+    from nano_ktrans_b200 import _lib
+
+    d = dict(num_experts=128, top_k=8, hidden_size=2048, inter_size=768, bits=4, group_size=128,
+             router_use_softmax=1, normalize_topk_prob=1, max_tokens=64, shared_inter=0)
+    d[field] = value
+    desc = _lib.MoeLayerDesc(*[d[n] for n in _lib._DESC_FIELDS])
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(256)
+    rc = lib.moe_create(ctypes.byref(desc), ctypes.byref(h), err, len(err))
+    assert rc == _lib.MOE_EINVAL
+    assert needle in err.value.decode()
+    assert not h.value
+
+
+def test_null_handle_calls_fail_cleanly(lib):
+    from nano_ktrans_b200 import _lib
+
+    assert lib.moe_route(None, None, 0, None, None, None) == _lib.MOE_EINVAL
+    assert lib.moe_experts_forward(None, None, None, None, 0, None, 0, None, None) == _lib.MOE_EINVAL
+    lib.moe_destroy(None)
+
+
+@pytest.mark.parametrize("bits,group", [(4, 128), (4, 64), (8, 0), (8, 128)])
+def test_torch_quantizer_matches_oracle(bits, group):
+    from nano_ktrans_b200.weights import quantize_symmetric
+
+    rng = np.random.Generator(np.random.PCG64(5))
+    w = rng.standard_normal((48, 256), dtype=np.float32) * np.float32(0.02)
+    q = quantize_symmetric(torch.from_numpy(w), group_size=group, bits=bits)
+    ref = mo.make_quant_linear(w, group if group else 256, bits)
+    np.testing.assert_array_equal(q.qweight.numpy(), ref.qweight)
+    np.testing.assert_array_equal(q.scales.numpy(), ref.scales)
+    np.testing.assert_array_equal(q.dequantize().numpy(), ref.dequantize())
+
+
+def test_device_layout_is_the_reference_word_bytes():
+    from nano_ktrans_b200.weights import quantize_symmetric, stack_layer
+
+    rng = np.random.Generator(np.random.PCG64(6))
+    experts = []
+    for _ in range(3):
+        experts.append({p: quantize_symmetric(torch.from_numpy(rng.standard_normal(s, dtype=np.float32) * 0.02),
+                                              group_size=64)
+                        for p, s in (("gate", (64, 256)), ("up", (64, 256)), ("down", (256, 64)))})
+    lw = stack_layer(experts, "cpu")
+    assert lw.gate_q.shape == (3, 64, 128) and lw.gate_q.dtype == torch.uint8
+    assert lw.down_s.shape == (3, 256, 1) and lw.down_s.dtype == torch.bfloat16
+    for e in range(3):
+        words = lw.gate_q[e].numpy().view(np.int32)
+        np.testing.assert_array_equal(words, experts[e]["gate"].qweight.numpy())
+        codes = mo.unpack_words(words, 4)
+        assert codes.shape == (64, 256)
+    assert lw.group_size == 64
+    assert lw.expert_bytes() == 2 * (64 * 128 + 64 * 4 * 2) + 256 * 32 + 256 * 1 * 2
+
+
+def test_gptq_loader_reads_reference_layout(tmp_path):
+    """The on-disk layout the reference's own loader test writes
+    (tests/test_quantized_ops.py:20-52 of nano-ktrans)."""
+    from safetensors.torch import save_file
+
+    from nano_ktrans_b200.weight_loader import ExpertWeightLoader
+    from nano_ktrans_b200.weights import quantize_symmetric
+
+    dense = torch.randn(32, 128, generator=torch.Generator().manual_seed(0))
+    q = quantize_symmetric(dense, group_size=64, scale_dtype=torch.float32)
+    save_file({
+        "model.layers.0.mlp.experts.0.gate_proj.qweight": q.qweight.t().contiguous(),
+        "model.layers.0.mlp.experts.0.gate_proj.scales": q.scales.t().contiguous(),
+        "model.layers.0.mlp.experts.0.gate_proj.g_idx": (torch.arange(128) // 64).to(torch.int32),
+    }, str(tmp_path / "model.safetensors"))
+    (tmp_path / "quantize_config.json").write_text(json.dumps({"bits": 4, "group_size": 64, "sym": True}))
+    loaded = ExpertWeightLoader(str(tmp_path)).load_gptq_expert_linear(layer_idx=0, expert_idx=0, proj_name="gate")
+    assert torch.equal(loaded.qweight, q.qweight)
+    assert torch.equal(loaded.scales, q.scales)
+    assert loaded.group_size == 64 and loaded.sym
+
+
+def test_loader_rejects_nonsequential_g_idx(tmp_path):
+    from safetensors.torch import save_file
+
+    from nano_ktrans_b200.weight_loader import ExpertWeightLoader
+    from nano_ktrans_b200.weights import quantize_symmetric
+
+    q = quantize_symmetric(torch.randn(16, 128), group_size=64)
+    g_idx = (torch.arange(128) // 64).flip(0).to(torch.int32)
+    save_file({"l.qweight": q.qweight.t().contiguous(), "l.scales": q.scales.t().contiguous(), "l.g_idx": g_idx},
+              str(tmp_path / "m.safetensors"))
+    (tmp_path / "quantize_config.json").write_text(json.dumps({"bits": 4, "group_size": 64}))
+    with pytest.raises(NotImplementedError):
+        ExpertWeightLoader(str(tmp_path)).load_gptq_linear("l")
+
+
+def test_backend_name_registry():
+    from nano_ktrans_b200 import normalize_offload_backend_name
+
+    assert normalize_offload_backend_name("cuda") == "cuda"
+    assert normalize_offload_backend_name("B200") == "cuda"
+    assert normalize_offload_backend_name(None) == "cpu"
+    assert normalize_offload_backend_name("pim-shadow") == "pim_shadow"
+    with pytest.raises(ValueError):
+        normalize_offload_backend_name("tpu")
+
+
+def test_moe_layer_refuses_cpu_tensors():
+    from nano_ktrans_b200.moe_layer import MoeLayer
+    from nano_ktrans_b200.weights import quantize_symmetric, stack_layer
+
+    ex = [{p: quantize_symmetric(torch.randn(*s) * 0.02, group_size=64) for p, s in
+           (("gate", (64, 256)), ("up", (64, 256)), ("down", (256, 64)))}]
+    with pytest.raises(ValueError, match="CUDA"):
+        MoeLayer(stack_layer(ex, "cpu"), top_k=1)
+
+
+def test_routing_oracle_properties():
+    rng = np.random.Generator(np.random.PCG64(3))
+    logits = mo.f32_to_bf16_bits(rng.standard_normal((64, 128), dtype=np.float32))
+    ids, w, probs = mo.route(logits, 8, True, True)
+    wf = mo.bf16_bits_to_f32(w)
+    assert np.all(np.diff(mo.bf16_bits_to_f32(probs)[np.arange(64)[:, None], ids], axis=1) <= 0)
+    np.testing.assert_allclose(wf.sum(1), 1.0, atol=2e-2)
+    ids2, w2, _ = mo.route(logits, 2, False, True)
+    np.testing.assert_allclose(mo.bf16_bits_to_f32(w2).sum(1), 1.0, atol=1e-2)
