@@ -140,18 +140,18 @@ class ClockSampler:
 def make_unique_layer(gen, device):
     import torch
 
-    from nano_ktrans_b200.weights import LayerWeights, quantize_symmetric
+    from nano_ktrans_b200.weights import LayerWeights, quantize_symmetric, scale_stride
 
     E, H, I, bits, g = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["bits"], CFG["group"]
     out = {}
     for proj, (n, k) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
         q = torch.empty(E, n, k * bits // 8, dtype=torch.uint8, device=device)
-        s = torch.empty(E, n, k // g, dtype=torch.bfloat16, device=device)
+        s = torch.zeros(E, n, scale_stride(k // g), dtype=torch.bfloat16, device=device)
         for e0 in range(0, E, 16):
             w = torch.randn(16 * n, k, generator=gen, device=device) * 0.02
             qw = quantize_symmetric(w, group_size=g, bits=bits)
             q[e0:e0 + 16] = qw.qweight.view(torch.uint8).view(16, n, -1)
-            s[e0:e0 + 16] = qw.scales.view(16, n, -1).to(torch.bfloat16)
+            s[e0:e0 + 16, :, :k // g] = qw.scales.view(16, n, -1).to(torch.bfloat16)
             del w, qw
         out[proj] = (q, s)
     return LayerWeights(bits=bits, group_size=g, gate_q=out["gate"][0], gate_s=out["gate"][1],
@@ -177,8 +177,8 @@ def make_inputs(gen, n_layers, batch, device):
 
 def expert_proj_bytes(lw):
     """Algorithmic bytes of one expert: (gate+up, down) codes + scales."""
-    gu = sum(t[0].numel() * t.element_size() for t in (lw.gate_q, lw.gate_s, lw.up_q, lw.up_s))
-    dn = sum(t[0].numel() * t.element_size() for t in (lw.down_q, lw.down_s))
+    gu = sum(q[0].numel() + q.shape[1] * lw.groups(q) * 2 for q in (lw.gate_q, lw.up_q))
+    dn = lw.down_q[0].numel() + lw.down_q.shape[1] * lw.groups(lw.down_q) * 2
     return gu, dn
 
 
@@ -314,8 +314,8 @@ def host_expert(lw, e):
     trip = []
     for q, s in ((lw.gate_q, lw.gate_s), (lw.up_q, lw.up_s), (lw.down_q, lw.down_s)):
         words = q[e].contiguous().cpu().numpy().view(np.int32)
-        sc = s[e].to(torch.float32).cpu().numpy()
         k = words.shape[1] * 32 // lw.bits
+        sc = s[e, :, :lw.groups(q)].to(torch.float32).cpu().numpy()
         trip.append(mo.QuantLinear(words, sc, g or k, lw.bits))
     return tuple(trip)
 
@@ -483,18 +483,23 @@ def main():
     L = args.layers
     steps_bytes = [distinct[i % L] * (gu_bytes + dn_bytes) for i in range(args.steps)]
 
+    # dominant kernel: the single-launch decode step when the batch fits it,
+    # else the gate/up matvec of the multi-kernel chain
+    fused = args.batch <= 4
+    kclass = _lib.K_DECODE_FUSED if fused else _lib.K_GATEUP
     with ClockSampler(local) as clk:
-        ms, k_ms, launches = run_device(layers, x, logits, outs, args.steps, args.warmup,
-                                        profile_layer_class=_lib.K_GATEUP)
+        ms, k_ms, launches = run_device(layers, x, logits, outs, args.steps, args.warmup, profile_layer_class=kclass)
     ms = max_over_ranks(ms)
     tokens = args.steps * args.batch * world
     value = tokens / (ms / 1e3)
     alg_bytes = sum(steps_bytes)
     gbs = alg_bytes * world / (ms / 1e3) / 1e9
-    # roofline of the dominant kernel (gate/up): its algorithmic bytes per launch / its event time
-    gu_per_launch = statistics.mean(d * gu_bytes for d in distinct)
-    achieved = gu_per_launch / (k_ms / 1e3) / 1e9
-    traffic = read_traffic("gateup", args.batch)
+    # roofline: the kernel's algorithmic bytes per launch (codes + scales of the
+    # distinct routed experts it reads) / its CUDA-event duration
+    per_launch = statistics.mean(d * ((gu_bytes + dn_bytes) if fused else gu_bytes) for d in distinct)
+    achieved = per_launch / (k_ms / 1e3) / 1e9
+    kname = "moe_decode_fused_kernel<4>" if fused else "expert_matvec_kernel<4,32,gate/up>"
+    traffic = read_traffic("decode_fused" if fused else "gateup", args.batch)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -502,9 +507,9 @@ def main():
         "vs_baseline": None, "dtype": "u4 codes, f32 accumulate, bf16 io", "data": "synthetic",
         "config": config_block(args, world),
         "expert_weight_gbs": gbs, "expert_weight_frac_of_peak": gbs / world / peak,
-        "roofline": {"bound": "hbm", "kernel": "expert_matvec_kernel<4,32,gate/up>", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-                     "traffic": traffic, "algorithmic_bytes_per_launch": gu_per_launch,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": per_launch,
                      "avg_launch_ms": k_ms},
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),

@@ -41,7 +41,10 @@
  *                              reference GPTQLinearWeight.qweight int32 words
  *                              [N, K*bits/32] (codes LSB-first along K,
  *                              offset-binary, zero point 2^(bits-1));
- *   s[e][n][K/group] bf16    — per-group scales.
+ *   s[e][n][SS] bf16         — per-group scales, SS = K/group rounded up to
+ *                              a multiple of 8 (each scale row is 16-byte
+ *                              aligned so it can be bulk-copied; the padding
+ *                              is never read).
  *   gate/up: N = inter, K = hidden.  down: N = hidden, K = inter.
  */
 #ifndef MOE_B200_H
@@ -151,8 +154,20 @@ enum moe_kernel_class {
   MOE_K_PERMUTE = 2,
   MOE_K_GATEUP = 3,
   MOE_K_DOWN = 4,
-  MOE_K_COMBINE = 5
+  MOE_K_COMBINE = 5,
+  MOE_K_DECODE_FUSED = 6 /* single-launch decode step (route + experts + combine) */
 };
+
+/* Handle options for moe_set_option. */
+enum moe_option {
+  /* 1 (default): batches small enough run as one cooperative launch;
+   * 0: always use the multi-kernel path. */
+  MOE_OPT_DECODE_FUSED = 1
+};
+
+/* Set a handle option (no counterpart in the reference: selects between two
+ * device implementations of the same step). */
+int moe_set_option(void* handle, int32_t option, int32_t value);
 
 /* Bracket the launch of one kernel class with CUDA events on the launching
  * stream in each of the next `max_samples` forward calls (no counterpart in

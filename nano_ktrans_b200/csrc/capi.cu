@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "../../include/moe_b200.h"
+#include "common.cuh"
 #include "kernels.h"
 
 namespace {
@@ -38,6 +39,8 @@ struct Handle {
   float* sh_g = nullptr;   // [max_tokens]
   int64_t* ids_tmp = nullptr;
   uint16_t* w_tmp = nullptr;
+  unsigned* grid_bar = nullptr;  // [2] grid-barrier state of the fused decode kernel
+  bool decode_fused = true;
   std::string err;
   int last_launches = 0;
   // profiling: events bracketing one kernel class
@@ -47,9 +50,18 @@ struct Handle {
   std::vector<cudaEvent_t> prof_ev;
 };
 
+// Under stream capture a plain event record only becomes a dependency marker;
+// the external flag makes it a real event-record node of the graph, so the
+// bracketed kernel can be timed on every replay.
 void prof_mark(Handle* h, int cls, bool after, cudaStream_t st) {
   if (h->prof_class != cls || h->prof_n >= h->prof_max) return;
-  cudaEventRecord(h->prof_ev[2 * h->prof_n + (after ? 1 : 0)], st);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cap);
+  cudaEvent_t ev = h->prof_ev[2 * h->prof_n + (after ? 1 : 0)];
+  if (cap == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, st);
   if (after) ++h->prof_n;
 }
 
@@ -86,6 +98,7 @@ QuantProj make_proj(const Handle* h, const void* q, const void* s, int n, int k)
   p.n = n;
   p.k = k;
   p.group = proj_group(h->d, k);
+  p.sstride = (k / p.group + 7) / 8 * 8;
   return p;
 }
 
@@ -140,7 +153,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   const size_t o_status = take(4), o_counts = take(4 * E), o_offsets = take(4 * (E + 1)), o_active = take(4 * E),
                o_nact = take(4), o_sorted = take(4 * P), o_pos = take(4 * P), o_h = take(4 * P * I),
                o_y = take(4 * P * H), o_shh = take(S ? 4 * T * S : 0), o_shy = take(S ? 4 * T * H : 0),
-               o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P);
+               o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P), o_bar = take(8);
   h->ws_bytes = off;
   cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
   if (e != cudaSuccess) {
@@ -165,6 +178,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   }
   h->ids_tmp = reinterpret_cast<int64_t*>(b + o_ids);
   h->w_tmp = reinterpret_cast<uint16_t*>(b + o_w);
+  h->grid_bar = reinterpret_cast<unsigned*>(b + o_bar);
   e = cudaMemset(h->ws, 0, h->ws_bytes);
   if (e != cudaSuccess) {
     fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
@@ -219,10 +233,55 @@ int moe_route(void* handle, const uint16_t* logits_dev, int32_t T, int64_t* ids_
   return check_launch(h, "moe_route");
 }
 
+// The single-launch decode kernel, when the batch is small enough and no
+// shared expert is requested.  `logits` set: route in-kernel, writing
+// ids_out/w_out; otherwise ids/wts are the given routing.  Returns true when
+// launched.
+static bool try_decode_fused(Handle* h, const uint16_t* x, const uint16_t* logits, const int64_t* ids,
+                             const uint16_t* wts, int64_t* ids_out, uint16_t* w_out, int T, const uint8_t* mask,
+                             bool add_shared, uint16_t* out, cudaStream_t st) {
+  const moe_layer_desc& d = h->d;
+  if (!h->decode_fused || (add_shared && d.shared_inter > 0)) return false;
+  const int H = d.hidden_size, I = d.inter_size;
+  moe::DecodeFusedParams p{};
+  p.gate = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H);
+  p.up = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H);
+  p.down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
+  if (!moe::decode_fused_eligible(d.bits, T, d.num_experts, d.top_k, p.gate, p.down, h->num_sms)) return false;
+  p.x = x;
+  p.logits = logits;
+  p.ids_in = logits ? nullptr : ids;
+  p.w_in = logits ? nullptr : wts;
+  p.mask = mask;
+  p.ids_out = ids_out;
+  p.w_out = w_out;
+  p.T = T;
+  p.E = d.num_experts;
+  p.top_k = d.top_k;
+  p.use_softmax = d.router_use_softmax;
+  p.renorm = d.normalize_topk_prob;
+  p.hbuf = h->hbuf;
+  p.out = out;
+  p.bar = h->grid_bar;
+  p.status = h->rt.status;
+  p.num_sms = h->num_sms;
+  prof_mark(h, MOE_K_DECODE_FUSED, false, st);
+  const int rc = moe::launch_decode_fused(d.bits, p, st);
+  prof_mark(h, MOE_K_DECODE_FUSED, true, st);
+  if (rc < 0) {
+    cudaGetLastError();  // a refused launch configuration is not sticky; use the multi-kernel path
+    return false;
+  }
+  h->last_launches = 1;
+  return true;
+}
+
 static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, const uint16_t* wts, int T,
                            const uint8_t* mask, bool add_shared, uint16_t* out, cudaStream_t st, int launches) {
   const moe_layer_desc& d = h->d;
   const int E = d.num_experts, H = d.hidden_size, I = d.inter_size, k = d.top_k;
+  if (launches == 0 && try_decode_fused(h, x, nullptr, ids, wts, nullptr, nullptr, T, mask, add_shared, out, st))
+    return check_launch(h, "moe_experts_forward");
   prof_mark(h, MOE_K_PERMUTE, false, st);
   moe::launch_permute(ids, T, k, E, mask, h->rt, st);
   prof_mark(h, MOE_K_PERMUTE, true, st);
@@ -290,6 +349,8 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
   int64_t* ids = ids_dev ? ids_dev : h->ids_tmp;
   uint16_t* wts = w_dev ? w_dev : h->w_tmp;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (try_decode_fused(h, x_dev, logits_dev, nullptr, nullptr, ids, wts, T, nullptr, true, out_dev, st))
+    return check_launch(h, "moe_forward");
   prof_mark(h, MOE_K_ROUTE, false, st);
   moe::launch_route(logits_dev, T, h->d.num_experts, h->d.top_k, h->d.router_use_softmax != 0,
                     h->d.normalize_topk_prob != 0, ids, wts, st);
@@ -333,8 +394,19 @@ int moe_read_status(void* handle, int32_t* status, void* stream) {
   cudaError_t e = cudaMemcpyAsync(status, h->rt.status, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e == cudaSuccess) e = cudaMemsetAsync(h->rt.status, 0, sizeof(int32_t), st);
+  // a timed-out grid barrier may have left its arrival count behind: reset it
+  if (e == cudaSuccess && (*status & moe::kStatusTimeout)) e = cudaMemsetAsync(h->grid_bar, 0, 8, st);
   if (e != cudaSuccess) return fail(h, MOE_ECUDA, "moe_read_status: %s", cudaGetErrorString(e));
   return MOE_OK;
+}
+
+int moe_set_option(void* handle, int32_t option, int32_t value) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  switch (option) {
+    case MOE_OPT_DECODE_FUSED: h->decode_fused = value != 0; return MOE_OK;
+    default: return fail(h, MOE_EINVAL, "moe_set_option: unknown option %d", option);
+  }
 }
 
 int moe_last_launch_count(void* handle) {
@@ -345,7 +417,7 @@ int moe_last_launch_count(void* handle) {
 int moe_profile_begin(void* handle, int32_t kernel_class, int32_t max_samples) {
   Handle* h = static_cast<Handle*>(handle);
   if (h == nullptr) return MOE_EINVAL;
-  if (kernel_class < MOE_K_ROUTE || kernel_class > MOE_K_COMBINE || max_samples < 1)
+  if (kernel_class < MOE_K_ROUTE || kernel_class > MOE_K_DECODE_FUSED || max_samples < 1)
     return fail(h, MOE_EINVAL, "moe_profile_begin: bad kernel class or sample count");
   for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
   h->prof_ev.assign(2 * static_cast<size_t>(max_samples), nullptr);
@@ -363,10 +435,11 @@ int moe_profile_end(void* handle, float* total_ms, int32_t* samples) {
   if (h == nullptr || total_ms == nullptr || samples == nullptr) return MOE_EINVAL;
   double sum = 0.0;
   for (int i = 0; i < h->prof_n; ++i) {
-    if (cudaEventSynchronize(h->prof_ev[2 * i + 1]) != cudaSuccess) return fail(h, MOE_ECUDA, "event sync failed");
+    cudaError_t e = cudaEventSynchronize(h->prof_ev[2 * i + 1]);
+    if (e != cudaSuccess) return fail(h, MOE_ECUDA, "moe_profile_end: event sync: %s", cudaGetErrorString(e));
     float ms = 0.f;
-    if (cudaEventElapsedTime(&ms, h->prof_ev[2 * i], h->prof_ev[2 * i + 1]) != cudaSuccess)
-      return fail(h, MOE_ECUDA, "cudaEventElapsedTime failed");
+    e = cudaEventElapsedTime(&ms, h->prof_ev[2 * i], h->prof_ev[2 * i + 1]);
+    if (e != cudaSuccess) return fail(h, MOE_ECUDA, "moe_profile_end: elapsed time: %s", cudaGetErrorString(e));
     sum += ms;
   }
   *total_ms = static_cast<float>(sum);

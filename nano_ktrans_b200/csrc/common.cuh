@@ -32,7 +32,8 @@
 namespace moe {
 
 constexpr uint32_t kFullMask = 0xffffffffu;
-constexpr int kStatusBadExpertId = 1;
+constexpr int kStatusBadExpertId = 1;  // an expert id outside [0, E) was skipped
+constexpr int kStatusTimeout = 2;      // a bounded wait expired; outputs of that call are invalid
 
 MOE_DEV float bf16_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
 

@@ -55,8 +55,11 @@ __global__ void __launch_bounds__(kThreads) expert_matvec_kernel(MatvecArgs a) {
   const int K4 = K / 4;
   const int nchunks = K / kCodes;
   const int chunk_iters = (nchunks + LPR - 1) / LPR;
+  // per-token stride of the interleaved activation layout, padded to whole
+  // LPR-chunk groups so the last partial group stays inside its token's slot
+  const int K4p = chunk_iters * LPR * kQ;
   const size_t row_bytes = static_cast<size_t>(K) * BITS / 8;
-  const int G = K / a.p0.group;
+  const int G = a.p0.sstride;
   const int tiles_per_expert = (N + kRowsPerTile - 1) / kRowsPerTile;
   const int n_act = a.identity_tokens > 0 ? 1 : *a.n_active;
   const int total = n_act * tiles_per_expert;
@@ -108,7 +111,7 @@ __global__ void __launch_bounds__(kThreads) expert_matvec_kernel(MatvecArgs a) {
         v.y *= act_prescale<BITS>(k0 + 1);
         v.z *= act_prescale<BITS>(k0 + 2);
         v.w *= act_prescale<BITS>(k0 + 3);
-        xs4[tt * K4 + ((c / LPR) * kQ + q) * LPR + (c % LPR)] = v;
+        xs4[tt * K4p + ((c / LPR) * kQ + q) * LPR + (c % LPR)] = v;
       }
       __syncthreads();
 
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) expert_matvec_kernel(MatvecArgs a) {
 #pragma unroll
             for (int t = 0; t < kMaxTch; ++t) {
               if (t < nt) {
-                const float4* xt = xb + t * K4;
+                const float4* xt = xb + t * K4p;
                 acc0[t] = fmaf(s0v, chunk_dot<BITS>(wv0, xt, LPR), acc0[t]);
                 if constexpr (GATEUP) acc1[t] = fmaf(s1v, chunk_dot<BITS>(wv1, xt, LPR), acc1[t]);
               }
@@ -161,17 +164,36 @@ __global__ void __launch_bounds__(kThreads) expert_matvec_kernel(MatvecArgs a) {
   }
 }
 
+constexpr int kSmemLimit = 227 * 1024;
+
+// Shared-memory bytes per staged token: K fp32 activations, padded to whole
+// groups of LPR chunks.
+template <int BITS, int LPR>
+static size_t token_smem_bytes(int K) {
+  constexpr int kCodes = ChunkTraits<BITS>::kCodes;
+  const int nchunks = K / kCodes;
+  const int chunk_iters = (nchunks + LPR - 1) / LPR;
+  return static_cast<size_t>(chunk_iters) * LPR * kCodes * sizeof(float);
+}
+
+template <int BITS, int LPR>
+static int pick_tch(int K) {
+  const size_t per = token_smem_bytes<BITS, LPR>(K);
+  return static_cast<int>(std::max<size_t>(1, std::min<size_t>(kMaxTch, kSmemLimit / per)));
+}
+
 template <int BITS, int LPR, bool GATEUP>
-static int launch_mv(const MatvecArgs& a, int max_active, int num_sms, cudaStream_t st) {
+static int launch_mv(MatvecArgs a, int max_active, int num_sms, cudaStream_t st) {
   constexpr int kRowsPerTile = kWarps * (32 / LPR);
   const int K = a.p0.k;
-  const size_t smem = static_cast<size_t>(a.tch) * K * sizeof(float);
+  a.tch = pick_tch<BITS, LPR>(K);
+  const size_t smem = static_cast<size_t>(a.tch) * token_smem_bytes<BITS, LPR>(K);
   static int configured_mask = 0;  // per device bit
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured_mask & (1 << dev))) {
     cudaFuncSetAttribute(expert_matvec_kernel<BITS, LPR, GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         200 * 1024);
+                         kSmemLimit);
     configured_mask |= 1 << dev;
   }
   const int tiles = max_active * ((a.p0.n + kRowsPerTile - 1) / kRowsPerTile);
@@ -180,14 +202,8 @@ static int launch_mv(const MatvecArgs& a, int max_active, int num_sms, cudaStrea
   return 1;
 }
 
-static int pick_tch(int K) {
-  const int budget = 192 * 1024;
-  return std::max(1, std::min(kMaxTch, budget / (K * static_cast<int>(sizeof(float)))));
-}
-
 template <bool GATEUP>
 static int dispatch(int bits, MatvecArgs& a, int max_active, int num_sms, cudaStream_t st) {
-  a.tch = pick_tch(a.p0.k);
   const int chunks = a.p0.k * bits / 128;
   const bool wide = chunks >= 64;
   if (bits == 4) {
@@ -331,8 +347,7 @@ __global__ void dequant_rows_kernel(QuantProj p, int expert, int row0, int nrows
   const int r = idx / words, wi = idx - r * words;
   const size_t rix = static_cast<size_t>(expert) * p.n + row0 + r;
   const uint32_t w = reinterpret_cast<const uint32_t*>(p.q + rix * (static_cast<size_t>(p.k) * BITS / 8))[wi];
-  const int G = p.k / p.group;
-  const float s = bf16_to_f32(p.s[rix * G + (wi * kVpw) / p.group]);
+  const float s = bf16_to_f32(p.s[rix * p.sstride + (wi * kVpw) / p.group]);
   float* o = out + static_cast<size_t>(r) * p.k + wi * kVpw;
   if constexpr (BITS == 4) {
     float2 d[4];

@@ -24,6 +24,7 @@ struct QuantProj {
   int n;           // output rows
   int k;           // input dim
   int group;       // group size along K (== k for per-channel)
+  int sstride;     // bf16 elements per scale row: K/group rounded up to 8 (16 bytes)
 };
 
 void launch_route(const uint16_t* logits, int T, int E, int top_k, bool use_softmax, bool renorm,
@@ -51,6 +52,28 @@ void launch_combine(const int64_t* ids, const uint16_t* weights, const RouteTabl
 
 // sg[t] = sigmoid(x[t] . g) for the shared expert's gate.
 void launch_shared_gate(const uint16_t* x, const uint16_t* g, int T, int H, float* sg, cudaStream_t st);
+
+// Single-launch decode step (decode_fused.cu).
+struct DecodeFusedParams {
+  const uint16_t* x;
+  const uint16_t* logits;   // routing computed in-kernel when ids_in == nullptr
+  const int64_t* ids_in;
+  const uint16_t* w_in;
+  const uint8_t* mask;
+  int64_t* ids_out;
+  uint16_t* w_out;
+  QuantProj gate, up, down;
+  int T, E, top_k, use_softmax, renorm;
+  float* hbuf;
+  uint16_t* out;
+  unsigned* bar;  // 2 words, zero-initialised grid-barrier state
+  int* status;
+  int num_sms;
+};
+bool decode_fused_eligible(int bits, int T, int E, int top_k, const QuantProj& gate, const QuantProj& down,
+                           int num_sms);
+// 1 = launched; negative = not launched (caller uses the multi-kernel path).
+int launch_decode_fused(int bits, const DecodeFusedParams& p, cudaStream_t st);
 
 void launch_dequant_rows(int bits, const QuantProj& p, int expert, int row0, int nrows, float* out,
                          cudaStream_t st);

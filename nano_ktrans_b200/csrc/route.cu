@@ -1,13 +1,7 @@
 // route.cu — router top-k (K1) and the token -> expert permutation (K1b).
 //
-// K1 follows nano_ktrans/layers/hybrid_moe.py:3321-3329:
-//   softmax routing (Qwen2/Qwen3): p = bf16(softmax_fp32(logits)),
-//     (w, ids) = topk(p, k), and if normalize_topk_prob:
-//     w = bf16(w / bf16(sum(w)))   (bf16 tensor ops: fp32 math, bf16 result)
-//   Mixtral routing: (w, ids) = topk(logits, k); w = bf16(softmax_fp32(w)).
-// One warp per token; each lane holds experts lane, lane+32, ...  Ties are
-// broken by (value desc, expert index asc); NaN ranks above every number, as
-// in torch.topk.
+// K1 follows nano_ktrans/layers/hybrid_moe.py:3321-3329 with one warp per
+// token (route_warp.cuh holds the arithmetic and the tie rule).
 //
 // K1b replaces the reference's per-expert scan `topk_ids == e` over all E
 // experts (nano_ktrans/kernels/cpu_moe.py:515-527) with one stable counting
@@ -18,15 +12,9 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "route_warp.cuh"
 
 namespace moe {
-
-MOE_DEV bool rank_before(float a, int ia, float b, int ib) {
-  const bool na = isnan(a), nb = isnan(b);
-  if (na != nb) return na;
-  if (!na && a != b) return a > b;
-  return ia < ib;
-}
 
 template <int EPL>
 __global__ void __launch_bounds__(256) route_kernel(const uint16_t* __restrict__ logits, int T, int E, int top_k,
@@ -35,81 +23,11 @@ __global__ void __launch_bounds__(256) route_kernel(const uint16_t* __restrict__
   const int token = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (token >= T) return;
-  const uint16_t* row = logits + static_cast<size_t>(token) * E;
-  float v[EPL];
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const int e = i * 32 + lane;
-    v[i] = e < E ? bf16_to_f32(row[e]) : 0.0f;
-  }
-  if (use_softmax) {
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < EPL; ++i)
-      if (i * 32 + lane < E) m = fmaxf(m, v[i]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      if (i * 32 + lane < E) {
-        v[i] = expf(v[i] - m);
-        s += v[i];
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(kFullMask, s, off);
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) v[i] = round_bf16(v[i] / s);
-  }
-
-  // top-k by repeated warp arg-max; lane j keeps the j-th pick
-  uint32_t taken = 0;
-  float my_val = 0.0f;
-  int my_id = 0;
-  for (int j = 0; j < top_k; ++j) {
-    float bv = 0.0f;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      const int e = i * 32 + lane;
-      if (e < E && !((taken >> i) & 1u) && (bi == 0x7fffffff || rank_before(v[i], e, bv, bi))) {
-        bv = v[i];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(kFullMask, bv, off);
-      const int oi = __shfl_xor_sync(kFullMask, bi, off);
-      if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ov, oi, bv, bi))) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-    if (lane == j) {
-      my_val = bv;
-      my_id = bi;
-    }
-  }
-
-  float w = my_val;
-  if (use_softmax) {
-    if (renorm) {
-      float s = 0.0f;  // sequential sum in slot order, fp32 (bf16 sum accumulates in fp32)
-      for (int j = 0; j < top_k; ++j) s += __shfl_sync(kFullMask, my_val, j);
-      w = my_val / round_bf16(s);
-    }
-  } else {
-    const float m = __shfl_sync(kFullMask, my_val, 0);
-    const float ex = lane < top_k ? expf(my_val - m) : 0.0f;
-    float s = 0.0f;
-    for (int j = 0; j < top_k; ++j) s += __shfl_sync(kFullMask, ex, j);
-    w = ex / s;
-  }
+  int id;
+  float w;
+  route_token_warp<EPL>(logits + static_cast<size_t>(token) * E, E, top_k, use_softmax != 0, renorm != 0, id, w);
   if (lane < top_k) {
-    ids[static_cast<size_t>(token) * top_k + lane] = my_id;
+    ids[static_cast<size_t>(token) * top_k + lane] = id;
     weights[static_cast<size_t>(token) * top_k + lane] = f32_to_bf16(w);
   }
 }

@@ -146,6 +146,11 @@ class MoeLayer:
                    "moe_read_status")
         return int(st.value)
 
+    def set_decode_fused(self, enabled: bool) -> None:
+        """Run small batches as one cooperative launch (default) or always as the multi-kernel chain."""
+        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_DECODE_FUSED, int(bool(enabled))), self._h,
+                   "moe_set_option")
+
     def profile_begin(self, kernel_class: int, max_samples: int) -> None:
         _lib.check(_lib.lib().moe_profile_begin(self._h, kernel_class, max_samples), self._h, "moe_profile_begin")
 

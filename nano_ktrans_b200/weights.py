@@ -13,7 +13,7 @@ bit-width generic), with an option to round the stored scales to bf16.
 ``LayerWeights`` is the device layout the kernels read: for each projection
 the qweight bytes stacked over experts, ``uint8 [E, N, K*bits/8]`` (exactly
 the little-endian bytes of the int32 words, so no repacking), and the scales
-as ``bf16 [E, N, K/group]``.
+as ``bf16 [E, N, SS]`` with SS = K/group rounded up to 8 (16-byte rows).
 """
 from __future__ import annotations
 
@@ -107,6 +107,19 @@ def quantize_symmetric(weight: torch.Tensor, *, group_size: int = 128, bits: int
                             group_size=g, bits=bits, sym=True, linear_prefix=linear_prefix)
 
 
+def scale_stride(num_groups: int) -> int:
+    """bf16 scale elements per row on the device: groups rounded up to 8 (16 bytes)."""
+    return (num_groups + 7) // 8 * 8
+
+
+def pad_scales(s: torch.Tensor) -> torch.Tensor:
+    """[..., G] -> [..., scale_stride(G)] bf16, zero padding."""
+    g = s.shape[-1]
+    out = torch.zeros(*s.shape[:-1], scale_stride(g), dtype=torch.bfloat16, device=s.device)
+    out[..., :g] = s.to(torch.bfloat16)
+    return out
+
+
 def _codes_bytes(w: GPTQLinearWeight) -> torch.Tensor:
     return w.qweight.contiguous().view(torch.uint8)
 
@@ -154,15 +167,20 @@ class LayerWeights:
     def expert_bytes(self) -> int:
         """Packed code + scale bytes of one routed expert (all three projections)."""
         per = 0
-        for t in (self.gate_q, self.gate_s, self.up_q, self.up_s, self.down_q, self.down_s):
-            per += t[0].numel() * t.element_size()
+        for q, s in ((self.gate_q, self.gate_s), (self.up_q, self.up_s), (self.down_q, self.down_s)):
+            per += q[0].numel() + q.shape[1] * self.groups(q) * 2
         return per
+
+    def groups(self, q: torch.Tensor) -> int:
+        """Scale groups per row of a projection whose codes are ``q``."""
+        k = q.shape[2] * 8 // self.bits
+        return 1 if self.group_size == 0 else k // self.group_size
 
     def shared_bytes(self) -> int:
         if self.shared is None:
             return 0
-        return sum(self.shared[k].numel() * self.shared[k].element_size()
-                   for k in ("gate_q", "gate_s", "up_q", "up_s", "down_q", "down_s"))
+        return sum(self.shared[p + "_q"].numel() + self.shared[p + "_q"].shape[1] * self.groups(self.shared[p + "_q"]) * 2
+                   for p in ("gate", "up", "down"))
 
 
 def layer_group_size(experts: list[dict]) -> int:
@@ -195,7 +213,7 @@ def stack_layer(experts: list[dict], device, shared: Optional[dict] = None,
     def stack(proj: str):
         q = torch.stack([_codes_bytes(ex[proj]) for ex in experts]).to(device).contiguous()
         s = torch.stack([ex[proj].scales.to(torch.float32) for ex in experts])
-        return q, s.to(torch.bfloat16).to(device).contiguous()
+        return q, pad_scales(s).to(device).contiguous()
 
     gq, gsc = stack("gate")
     uq, usc = stack("up")
@@ -211,7 +229,7 @@ def stack_layer(experts: list[dict], device, shared: Optional[dict] = None,
         sh = {}
         for p in ("gate", "up", "down"):
             sh[p + "_q"] = _codes_bytes(shared[p]).unsqueeze(0).to(device).contiguous()
-            sh[p + "_s"] = shared[p].scales.to(torch.float32).unsqueeze(0).to(torch.bfloat16).to(device).contiguous()
+            sh[p + "_s"] = pad_scales(shared[p].scales.to(torch.float32).unsqueeze(0)).to(device).contiguous()
         sh["gate_vec"] = shared_gate_vec.reshape(-1).to(torch.bfloat16).to(device).contiguous()
     return LayerWeights(bits=bits, group_size=group, gate_q=gq, gate_s=gsc, up_q=uq, up_s=usc,
                         down_q=dq, down_s=dsc, shared=sh)

@@ -218,7 +218,8 @@ def offload_forward_f32(x_bf16: np.ndarray, topk_ids: np.ndarray, topk_w_bf16: n
     w = bf16_bits_to_f32(topk_w_bf16)
     t, h = x.shape
     out = np.zeros((t, h), dtype=np.float32)
-    num_experts = len(experts)
+    # experts may hold only the routed subset; scan every id that can occur
+    num_experts = max(max(experts) + 1, int(topk_ids.max()) + 1 if topk_ids.size else 0)
     for e in range(num_experts):
         if offload_mask is not None and not offload_mask[e]:
             continue
@@ -226,6 +227,8 @@ def offload_forward_f32(x_bf16: np.ndarray, topk_ids: np.ndarray, topk_w_bf16: n
         rows = np.nonzero(match.any(axis=1))[0]
         if rows.size == 0:
             continue
+        if e not in experts:
+            raise KeyError(f"expert {e} is routed but its weights were not provided")
         y = expert_forward(x[rows], *experts[e])
         r_idx, c_idx = np.nonzero(match[rows])
         wt = w[rows[r_idx], c_idx][:, None]

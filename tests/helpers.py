@@ -49,15 +49,15 @@ def device_layer(experts: dict, num_experts: int, hidden: int, inter: int, bits:
 
     def alloc(n, k, g):
         return (np.zeros((num_experts, n, k * bits // 8), dtype=np.uint8),
-                np.zeros((num_experts, n, g), dtype=np.float32))
+                np.zeros((num_experts, n, (g + 7) // 8 * 8), dtype=np.float32))
 
     gq, gs = alloc(inter, hidden, g_h)
     uq, us = alloc(inter, hidden, g_h)
     dq, ds = alloc(hidden, inter, g_i)
     for e, (g, u, d) in experts.items():
-        gq[e], gs[e] = g.qweight.view(np.uint8), g.scales
-        uq[e], us[e] = u.qweight.view(np.uint8), u.scales
-        dq[e], ds[e] = d.qweight.view(np.uint8), d.scales
+        gq[e], gs[e, :, :g_h] = g.qweight.view(np.uint8), g.scales
+        uq[e], us[e, :, :g_h] = u.qweight.view(np.uint8), u.scales
+        dq[e], ds[e, :, :g_i] = d.qweight.view(np.uint8), d.scales
 
     def tq(a):
         return torch.from_numpy(a).to(device)
@@ -70,7 +70,10 @@ def device_layer(experts: dict, num_experts: int, hidden: int, inter: int, bits:
         sh = {}
         for p, ql in zip(("gate", "up", "down"), shared):
             sh[p + "_q"] = tq(ql.qweight.view(np.uint8)[None].copy())
-            sh[p + "_s"] = ts(ql.scales[None].copy())
+            g = ql.scales.shape[1]
+            padded = np.zeros((1, ql.scales.shape[0], (g + 7) // 8 * 8), dtype=np.float32)
+            padded[0, :, :g] = ql.scales
+            sh[p + "_s"] = ts(padded)
         sh["gate_vec"] = torch.from_numpy(shared_gate_vec.view(np.int16).copy()).view(torch.bfloat16).to(device)
     return LayerWeights(bits=bits, group_size=group, gate_q=tq(gq), gate_s=ts(gs), up_q=tq(uq), up_s=ts(us),
                         down_q=tq(dq), down_s=ts(ds), shared=sh)

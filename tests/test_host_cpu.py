@@ -85,7 +85,7 @@ def test_device_layout_is_the_reference_word_bytes():
                         for p, s in (("gate", (64, 256)), ("up", (64, 256)), ("down", (256, 64)))})
     lw = stack_layer(experts, "cpu")
     assert lw.gate_q.shape == (3, 64, 128) and lw.gate_q.dtype == torch.uint8
-    assert lw.down_s.shape == (3, 256, 1) and lw.down_s.dtype == torch.bfloat16
+    assert lw.down_s.shape == (3, 256, 8) and lw.down_s.dtype == torch.bfloat16
     for e in range(3):
         words = lw.gate_q[e].numpy().view(np.int32)
         np.testing.assert_array_equal(words, experts[e]["gate"].qweight.numpy())

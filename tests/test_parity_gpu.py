@@ -58,9 +58,11 @@ def test_route_matches_reference(name, cuda_device):
             assert ref == mine, (t, ref, mine)
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
 @pytest.mark.parametrize("name", sorted(CASES))
-def test_experts_match_reference(name, cuda_device):
+def test_experts_match_reference(name, fused, cuda_device):
     g, c, _, layer = _golden_layer(name, cuda_device)
+    layer.set_decode_fused(fused)
     x = hp.bf16_tensor(g["x"], cuda_device)
     ids = torch.from_numpy(g["ids"]).to(cuda_device)
     w = hp.bf16_tensor(g["weights"], cuda_device)
@@ -98,7 +100,8 @@ def test_dequant_exhaustive_codes(bits, cuda_device):
     trip = []
     for n, k in ((I, H), (I, H), (H, I)):
         codes = rng.integers(0, n_codes, size=(n, k), dtype=np.uint8)
-        codes[0, :n_codes] = np.arange(n_codes)
+        m = min(n_codes, k)
+        codes[0, :m] = np.arange(m)
         codes[1, :] = np.arange(k) % n_codes
         g = 32 if bits == 4 else 16
         scales = mo.round_bf16(np.exp2(rng.uniform(-20, 4, size=(n, k // g))).astype(np.float32))
@@ -197,11 +200,14 @@ def _full_case(cfg, tokens, bits, group, seed, cuda_device, zipf=None, sample_to
                 check=check_tok, shared=shared, gate_vec=gate_vec)
 
 
-@pytest.mark.parametrize("tokens", [1, 8, 32, 64])
-def test_qwen3_w4_decode_sweep(tokens, cuda_device):
-    """Config 2: Qwen3-30B-A3B-shaped W4 g128 decode at batch 1/8/32/64."""
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+@pytest.mark.parametrize("tokens", [1, 3, 8, 32, 64])
+def test_qwen3_w4_decode_sweep(tokens, fused, cuda_device):
+    """Config 2: Qwen3-30B-A3B-shaped W4 g128 decode at batch 1/8/32/64 (and 3),
+    through the single-launch kernel (where the batch allows) and the chain."""
     d = _full_case(hp.QWEN3, tokens, 4, 128, 100 + tokens, cuda_device)
     layer = d["layer"]
+    layer.set_decode_fused(fused)
     ids, w = layer.route(hp.bf16_tensor(d["logits"], cuda_device))
     assert mo.tie_aware_match(ids.cpu().numpy(), d["ids"], d["ranked"]).all()
     x = hp.bf16_tensor(d["x"], cuda_device)
@@ -215,9 +221,11 @@ def test_qwen3_w4_decode_sweep(tokens, cuda_device):
     assert layer.read_status() == 0
 
 
-def test_qwen3_w8_per_channel_decode(cuda_device):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+def test_qwen3_w8_per_channel_decode(fused, cuda_device):
     """Config 1: W8 symmetric per-output-channel, batch 1."""
     d = _full_case(hp.QWEN3, 1, 8, 0, 7, cuda_device)
+    d["layer"].set_decode_fused(fused)
     out = d["layer"].forward(hp.bf16_tensor(d["x"], cuda_device), hp.bf16_tensor(d["logits"], cuda_device))
     torch.cuda.synchronize()
     ref = mo.offload_forward_f32(d["x"], d["ids"], d["w"], d["experts"])
@@ -241,22 +249,24 @@ def test_qwen2_shared_expert_zipf(cuda_device):
 # ---------------------------------------------------------------------------
 
 
-def test_deterministic_and_permutation_equivariant(cuda_device):
-    d = _full_case(hp.QWEN3, 32, 4, 128, 5, cuda_device)
+@pytest.mark.parametrize("tokens", [4, 32])
+def test_deterministic_and_permutation_equivariant(tokens, cuda_device):
+    d = _full_case(hp.QWEN3, tokens, 4, 128, 5, cuda_device)
     layer = d["layer"]
     x = hp.bf16_tensor(d["x"], cuda_device)
     lg = hp.bf16_tensor(d["logits"], cuda_device)
     a = layer.forward(x, lg).clone()
     b = layer.forward(x, lg).clone()
-    perm = torch.randperm(32, generator=torch.Generator().manual_seed(1)).to(cuda_device)
+    perm = torch.randperm(tokens, generator=torch.Generator().manual_seed(1)).to(cuda_device)
     c = layer.forward(x[perm].contiguous(), lg[perm].contiguous())
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert torch.equal(a[perm], c)
 
 
-def test_mask_split_sums_to_whole(cuda_device):
-    d = _full_case(hp.QWEN3, 8, 4, 128, 6, cuda_device)
+@pytest.mark.parametrize("tokens", [2, 8])
+def test_mask_split_sums_to_whole(tokens, cuda_device):
+    d = _full_case(hp.QWEN3, tokens, 4, 128, 6, cuda_device)
     layer = d["layer"]
     x = hp.bf16_tensor(d["x"], cuda_device)
     ids = torch.from_numpy(d["ids"]).to(cuda_device)
@@ -269,9 +279,11 @@ def test_mask_split_sums_to_whole(cuda_device):
     assert (whole - part).abs().max().item() <= 2 * whole.abs().max().item() * 2 ** -8
 
 
-def test_empty_and_bad_inputs(cuda_device):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+def test_empty_and_bad_inputs(fused, cuda_device):
     d = _full_case(hp.QWEN3, 4, 4, 128, 8, cuda_device)
     layer = d["layer"]
+    layer.set_decode_fused(fused)
     x = hp.bf16_tensor(d["x"], cuda_device)
     empty = layer.forward(x[:0], hp.bf16_tensor(d["logits"], cuda_device)[:0])
     assert empty.shape == (0, 2048)
@@ -302,3 +314,25 @@ def test_top_k_equals_num_experts(cuda_device):
     out = d["layer"].forward(hp.bf16_tensor(d["x"], cuda_device), hp.bf16_tensor(d["logits"], cuda_device))
     torch.cuda.synchronize()
     hp.assert_parity(hp.bf16_bits(out), mo.offload_forward_f32(d["x"], d["ids"], d["w"], d["experts"]))
+
+
+def test_fused_decode_is_one_launch_and_matches_chain(cuda_device):
+    """The single-launch decode step equals the multi-kernel chain bit for bit
+    on its routing and within fp32 summation order on its output."""
+    d = _full_case(hp.QWEN3, 2, 4, 128, 31, cuda_device)
+    layer = d["layer"]
+    x = hp.bf16_tensor(d["x"], cuda_device)
+    lg = hp.bf16_tensor(d["logits"], cuda_device)
+    ids_f = torch.empty(2, 8, dtype=torch.int64, device=cuda_device)
+    w_f = torch.empty(2, 8, dtype=torch.bfloat16, device=cuda_device)
+    fused = layer.forward(x, lg, out_ids=ids_f, out_weights=w_f).clone()
+    assert layer.last_launch_count() == 1
+    layer.set_decode_fused(False)
+    ids_c = torch.empty_like(ids_f)
+    w_c = torch.empty_like(w_f)
+    chain = layer.forward(x, lg, out_ids=ids_c, out_weights=w_c)
+    assert layer.last_launch_count() == 5
+    torch.cuda.synchronize()
+    assert torch.equal(ids_f, ids_c) and torch.equal(w_f, w_c)
+    assert torch.equal(fused, chain)
+    assert layer.read_status() == 0
