@@ -291,10 +291,10 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
   const QuantProj up = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H);
   const QuantProj down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
   prof_mark(h, MOE_K_GATEUP, false, st);
-  launches += moe::launch_gateup(d.bits, x, h->rt, k, max_active, 0, gate, up, h->hbuf, h->num_sms, st);
+  launches += moe::launch_gateup(d.bits, x, h->rt, k, max_active, T, 0, gate, up, h->hbuf, h->num_sms, st);
   prof_mark(h, MOE_K_GATEUP, true, st);
   prof_mark(h, MOE_K_DOWN, false, st);
-  launches += moe::launch_down(d.bits, h->hbuf, h->rt, max_active, 0, down, h->ybuf, h->num_sms, st);
+  launches += moe::launch_down(d.bits, h->hbuf, h->rt, max_active, T, 0, down, h->ybuf, h->num_sms, st);
   prof_mark(h, MOE_K_DOWN, true, st);
   const float* sg = nullptr;
   const float* sy = nullptr;
@@ -305,8 +305,8 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     const QuantProj sdp = make_proj(h, h->w.shared_down_q_dev, h->w.shared_down_s_dev, H, S);
     moe::launch_shared_gate(x, static_cast<const uint16_t*>(h->w.shared_gate_vec_dev), T, H, h->sh_g, st);
     ++launches;
-    launches += moe::launch_gateup(d.bits, x, h->rt, 1, 1, T, sgp, sup, h->sh_h, h->num_sms, st);
-    launches += moe::launch_down(d.bits, h->sh_h, h->rt, 1, T, sdp, h->sh_y, h->num_sms, st);
+    launches += moe::launch_gateup(d.bits, x, h->rt, 1, 1, T, T, sgp, sup, h->sh_h, h->num_sms, st);
+    launches += moe::launch_down(d.bits, h->sh_h, h->rt, 1, T, T, sdp, h->sh_y, h->num_sms, st);
     sg = h->sh_g;
     sy = h->sh_y;
   }

@@ -543,12 +543,17 @@ int launch_decode_fused(int bits, const DecodeFusedParams& p, cudaStream_t st) {
   if (smem > 227 * 1024) return -1;
 
   void (*kern)(FusedArgs) = bits == 4 ? moe_decode_fused_kernel<4> : moe_decode_fused_kernel<8>;
-  static int configured_mask[2] = {0, 0};
+  // opt in to exactly the dynamic shared memory this launch needs (the
+  // kernel's static shared memory counts against the same per-block limit)
+  static size_t configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured_mask[bits == 4 ? 0 : 1] & (1 << dev))) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    configured_mask[bits == 4 ? 0 : 1] |= 1 << dev;
+  size_t& have = configured[bits == 4 ? 0 : 1][dev & 63];
+  if (smem > have) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return -1;
+    have = smem;
   }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFThreads, smem) != cudaSuccess || per_sm < 1)

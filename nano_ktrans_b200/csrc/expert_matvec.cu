@@ -186,7 +186,7 @@ template <int BITS, int LPR, bool GATEUP>
 static int launch_mv(MatvecArgs a, int max_active, int num_sms, cudaStream_t st) {
   constexpr int kRowsPerTile = kWarps * (32 / LPR);
   const int K = a.p0.k;
-  a.tch = pick_tch<BITS, LPR>(K);
+  a.tch = std::max(1, std::min(pick_tch<BITS, LPR>(K), a.tch));  // caller set a.tch = tokens per expert bound
   const size_t smem = static_cast<size_t>(a.tch) * token_smem_bytes<BITS, LPR>(K);
   static int configured_mask = 0;  // per device bit
   int dev = 0;
@@ -214,7 +214,8 @@ static int dispatch(int bits, MatvecArgs& a, int max_active, int num_sms, cudaSt
               : launch_mv<8, 8, GATEUP>(a, max_active, num_sms, st);
 }
 
-int launch_gateup(int bits, const uint16_t* x, const RouteTables& rt, int top_k, int max_active, int identity_tokens,
+int launch_gateup(int bits, const uint16_t* x, const RouteTables& rt, int top_k, int max_active, int num_tokens,
+                  int identity_tokens,
                   const QuantProj& gate, const QuantProj& up, float* h, int num_sms, cudaStream_t st) {
   MatvecArgs a{};
   a.x = x;
@@ -227,10 +228,11 @@ int launch_gateup(int bits, const uint16_t* x, const RouteTables& rt, int top_k,
   a.p0 = gate;
   a.p1 = up;
   a.out = h;
+  a.tch = num_tokens;
   return dispatch<true>(bits, a, identity_tokens > 0 ? 1 : max_active, num_sms, st);
 }
 
-int launch_down(int bits, const float* h, const RouteTables& rt, int max_active, int identity_tokens,
+int launch_down(int bits, const float* h, const RouteTables& rt, int max_active, int num_tokens, int identity_tokens,
                 const QuantProj& down, float* y, int num_sms, cudaStream_t st) {
   MatvecArgs a{};
   a.h = h;
@@ -242,6 +244,7 @@ int launch_down(int bits, const float* h, const RouteTables& rt, int max_active,
   a.identity_tokens = identity_tokens;
   a.p0 = down;
   a.out = y;
+  a.tch = num_tokens;
   return dispatch<false>(bits, a, identity_tokens > 0 ? 1 : max_active, num_sms, st);
 }
 

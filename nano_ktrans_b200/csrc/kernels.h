@@ -37,12 +37,12 @@ void launch_permute(const int64_t* ids, int T, int top_k, int E, const uint8_t* 
 // h[s][n] for sorted positions s.  When identity_tokens > 0 the routing
 // tables are ignored and a single expert serves tokens 0..identity_tokens-1
 // (the shared expert), h indexed by token.
-int launch_gateup(int bits, const uint16_t* x, const RouteTables& rt, int top_k, int max_active,
+int launch_gateup(int bits, const uint16_t* x, const RouteTables& rt, int top_k, int max_active, int num_tokens,
                   int identity_tokens, const QuantProj& gate, const QuantProj& up, float* h,
                   int num_sms, cudaStream_t st);
 
 // down projection: y[s][n] = down_e(h[s]).
-int launch_down(int bits, const float* h, const RouteTables& rt, int max_active, int identity_tokens,
+int launch_down(int bits, const float* h, const RouteTables& rt, int max_active, int num_tokens, int identity_tokens,
                 const QuantProj& down, float* y, int num_sms, cudaStream_t st);
 
 // out[t][n] = bf16( sum_{slots by expert asc} w * y[pos] + sg[t] * ys[t][n] )
