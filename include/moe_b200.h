@@ -162,8 +162,18 @@ enum moe_kernel_class {
 enum moe_option {
   /* 1 (default): batches small enough run as one cooperative launch;
    * 0: always use the multi-kernel path. */
-  MOE_OPT_DECODE_FUSED = 1
+  MOE_OPT_DECODE_FUSED = 1,
+  /* 1: the single-launch decode kernel records per-CTA phase timestamps
+   * (allocates num_SMs * 8 * 8 bytes); read them with moe_read_trace. */
+  MOE_OPT_TRACE = 2
 };
+
+/* Copy the phase timestamps of the last traced single-launch decode step:
+ * out[c * 8 + i] = %globaltimer (ns) of CTA c at phase i (0 entry, 1 routing
+ * done, 2 gate/up done, 3 grid barrier passed, 4 intermediate staged, 5 exit).
+ * *n receives the CTA count.  Synchronises `stream`.  (No counterpart in the
+ * reference: tracing support.) */
+int moe_read_trace(void* handle, uint64_t* out, int32_t max_entries, int32_t* n, void* stream);
 
 /* Set a handle option (no counterpart in the reference: selects between two
  * device implementations of the same step). */

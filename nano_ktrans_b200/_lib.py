@@ -15,7 +15,7 @@ HEADER_PATH = os.path.join(os.path.dirname(PKG_DIR), "include", "moe_b200.h")
 
 MOE_OK, MOE_EINVAL, MOE_ECUDA, MOE_ENOWEIGHTS, MOE_ERANGE, MOE_EDEVICE = range(6)
 K_ROUTE, K_PERMUTE, K_GATEUP, K_DOWN, K_COMBINE, K_DECODE_FUSED = range(1, 7)
-OPT_DECODE_FUSED = 1
+OPT_DECODE_FUSED, OPT_TRACE = 1, 2
 
 _DESC_FIELDS = ("num_experts", "top_k", "hidden_size", "inter_size", "bits", "group_size",
                 "router_use_softmax", "normalize_topk_prob", "max_tokens", "shared_inter")
@@ -55,6 +55,7 @@ SIGNATURES = {
     "moe_last_launch_count": (_i32, [_vp]),
     "moe_profile_begin": (_i32, [_vp, _i32, _i32]),
     "moe_set_option": (_i32, [_vp, _i32, _i32]),
+    "moe_read_trace": (_i32, [_vp, ctypes.POINTER(ctypes.c_uint64), _i32, ctypes.POINTER(_i32), _vp]),
     "moe_profile_end": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_i32)]),
     "moe_last_error": (_i32, [_vp, _cp, _sz]),
     "moe_destroy": (None, [_vp]),

@@ -39,8 +39,9 @@ struct Handle {
   float* sh_g = nullptr;   // [max_tokens]
   int64_t* ids_tmp = nullptr;
   uint16_t* w_tmp = nullptr;
-  unsigned* grid_bar = nullptr;  // [2] grid-barrier state of the fused decode kernel
+  unsigned long long* grid_bar = nullptr;  // grid-barrier arrival counter of the fused decode kernel
   bool decode_fused = true;
+  unsigned long long* trace = nullptr;  // [num_sms][16] phase timestamps when tracing
   std::string err;
   int last_launches = 0;
   // profiling: events bracketing one kernel class
@@ -178,7 +179,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   }
   h->ids_tmp = reinterpret_cast<int64_t*>(b + o_ids);
   h->w_tmp = reinterpret_cast<uint16_t*>(b + o_w);
-  h->grid_bar = reinterpret_cast<unsigned*>(b + o_bar);
+  h->grid_bar = reinterpret_cast<unsigned long long*>(b + o_bar);
   e = cudaMemset(h->ws, 0, h->ws_bytes);
   if (e != cudaSuccess) {
     fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
@@ -263,6 +264,7 @@ static bool try_decode_fused(Handle* h, const uint16_t* x, const uint16_t* logit
   p.hbuf = h->hbuf;
   p.out = out;
   p.bar = h->grid_bar;
+  p.trace = h->trace;
   p.status = h->rt.status;
   p.num_sms = h->num_sms;
   prof_mark(h, MOE_K_DECODE_FUSED, false, st);
@@ -405,8 +407,32 @@ int moe_set_option(void* handle, int32_t option, int32_t value) {
   if (h == nullptr) return MOE_EINVAL;
   switch (option) {
     case MOE_OPT_DECODE_FUSED: h->decode_fused = value != 0; return MOE_OK;
+    case MOE_OPT_TRACE:
+      if (value && h->trace == nullptr) {
+        const size_t bytes = static_cast<size_t>(h->num_sms) * 16 * sizeof(unsigned long long);
+        cudaError_t e = cudaMalloc(&h->trace, bytes);
+        if (e == cudaSuccess) e = cudaMemset(h->trace, 0, bytes);
+        if (e != cudaSuccess) return fail(h, MOE_ECUDA, "moe_set_option(trace): %s", cudaGetErrorString(e));
+      } else if (!value && h->trace != nullptr) {
+        cudaFree(h->trace);
+        h->trace = nullptr;
+      }
+      return MOE_OK;
     default: return fail(h, MOE_EINVAL, "moe_set_option: unknown option %d", option);
   }
+}
+
+int moe_read_trace(void* handle, uint64_t* out, int32_t max_entries, int32_t* n, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr || out == nullptr || n == nullptr) return MOE_EINVAL;
+  if (h->trace == nullptr) return fail(h, MOE_EINVAL, "moe_read_trace: tracing is off");
+  const int entries = std::min(max_entries, h->num_sms * 16);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(out, h->trace, sizeof(uint64_t) * entries, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(h, MOE_ECUDA, "moe_read_trace: %s", cudaGetErrorString(e));
+  *n = h->num_sms;
+  return MOE_OK;
 }
 
 int moe_last_launch_count(void* handle) {
@@ -462,6 +488,7 @@ void moe_destroy(void* handle) {
   Handle* h = static_cast<Handle*>(handle);
   if (h == nullptr) return;
   for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
+  if (h->trace) cudaFree(h->trace);
   if (h->ws) cudaFree(h->ws);
   delete h;
 }

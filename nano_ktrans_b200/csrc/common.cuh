@@ -167,6 +167,66 @@ MOE_DEV float chunk_dot(uint4 wv, const float4* xs4, int stride4) {
   return acc.x + acc.y;
 }
 
+// ---------------------------------------------------------------------------
+// W4 with bf16 operands (gate/up, whose activations are bf16).
+//
+// Moving a nibble pair into bits 0-3 of each 16-bit half and OR-ing it into
+// 0x4300 (bf16 128.0, mantissa step 1) gives two exact bf16 values 128 + q per
+// logic op (a bf16 mantissa has 7 bits, so the nibble must sit in bits 0-3).
+// Every product x * (128 + q) is exact in the fp32 accumulator of
+// fma.rn.f32.bf16, and
+//   sum_j (q_j - 8) * x_j = sum_j x_j * (128 + q_j) - 136 * sum_j x_j,
+// the second term being one fp32 correction per chunk and token.
+// Per 8 weights: 3 shifts + 4 logic ops + 8 mixed-precision FMAs, against
+// 9 logic ops + 8 fp32 adds/FMAs for the fp32 unpack above.
+//
+// Activation operands of one word (codes k0..k0+7): the 4 bf16x2 registers
+// (x0, x4), (x1, x5), (x2, x6), (x3, x7) — matching the nibble pairs
+// (0,4) (1,5) (2,6) (3,7) of the word shifted right by 0, 4, 8 and 12 bits.
+// ---------------------------------------------------------------------------
+
+MOE_DEV uint32_t pack_bf16x2(uint16_t lo, uint16_t hi) { return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16); }
+
+// raw = 8 consecutive bf16 activations (x0..x7, two per 32-bit word, low half
+// first).  Returns the word's 4 operand registers; adds its share of the
+// chunk correction to `corr`.
+MOE_DEV uint4 w4_pack_x(uint4 raw, float& corr) {
+  const float x0 = __uint_as_float(raw.x << 16), x1 = __uint_as_float(raw.x & 0xffff0000u);
+  const float x2 = __uint_as_float(raw.y << 16), x3 = __uint_as_float(raw.y & 0xffff0000u);
+  const float x4 = __uint_as_float(raw.z << 16), x5 = __uint_as_float(raw.z & 0xffff0000u);
+  const float x6 = __uint_as_float(raw.w << 16), x7 = __uint_as_float(raw.w & 0xffff0000u);
+  corr += 136.0f * (((x0 + x1) + (x2 + x3)) + ((x4 + x5) + (x6 + x7)));
+  // (x0,x4) (x1,x5) (x2,x6) (x3,x7): byte permutes of the raw pairs
+  return make_uint4(__byte_perm(raw.x, raw.z, 0x5410), __byte_perm(raw.x, raw.z, 0x7632),
+                    __byte_perm(raw.y, raw.w, 0x5410), __byte_perm(raw.y, raw.w, 0x7632));
+}
+
+MOE_DEV void fma2_f32_bf16(float& a0, float& a1, uint32_t x, uint32_t v) {
+  asm("{\n\t.reg .b16 xl, xh, vl, vh;\n\tmov.b32 {xl, xh}, %2;\n\tmov.b32 {vl, vh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, xl, vl, %0;\n\tfma.rn.f32.bf16 %1, xh, vh, %1;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(x), "r"(v));
+}
+
+// Dot of one 16-byte W4 chunk (4 words, 32 codes) with its bf16 operands
+// (xq[q * stride4], q = 0..3), minus the chunk correction; unscaled by the
+// group scale.
+MOE_DEV float w4_chunk_dot_bf16(uint4 wv, const uint4* xq, int stride4, float corr) {
+  constexpr uint32_t M = 0x43004300u;
+  float a0 = 0.0f, a1 = 0.0f;
+  const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t ww = w[q];
+    const uint4 xv = xq[q * stride4];
+    fma2_f32_bf16(a0, a1, xv.x, (ww & 0x000F000Fu) | M);
+    fma2_f32_bf16(a0, a1, xv.y, ((ww >> 4) & 0x000F000Fu) | M);
+    fma2_f32_bf16(a0, a1, xv.z, ((ww >> 8) & 0x000F000Fu) | M);
+    fma2_f32_bf16(a0, a1, xv.w, ((ww >> 12) & 0x000F000Fu) | M);
+  }
+  return (a0 + a1) - corr;
+}
+
 MOE_DEV float silu_f32(float v) { return v / (1.0f + expf(-v)); }
 
 MOE_DEV float sigmoid_f32(float v) { return 1.0f / (1.0f + expf(-v)); }

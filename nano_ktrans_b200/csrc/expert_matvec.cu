@@ -58,6 +58,10 @@ __global__ void __launch_bounds__(kThreads) expert_matvec_kernel(MatvecArgs a) {
   // per-token stride of the interleaved activation layout, padded to whole
   // LPR-chunk groups so the last partial group stays inside its token's slot
   const int K4p = chunk_iters * LPR * kQ;
+  // W4 gate/up operands: [tch][Kw] uint4 words, then [tch][CW] chunk corrections
+  const int Kw = chunk_iters * LPR * 4, CW = chunk_iters * LPR;
+  uint4* xq = reinterpret_cast<uint4*>(xs4);
+  float* cq = reinterpret_cast<float*>(xq + a.tch * Kw);
   const size_t row_bytes = static_cast<size_t>(K) * BITS / 8;
   const int G = a.p0.sstride;
   const int tiles_per_expert = (N + kRowsPerTile - 1) / kRowsPerTile;
@@ -93,25 +97,47 @@ __global__ void __launch_bounds__(kThreads) expert_matvec_kernel(MatvecArgs a) {
     for (int tb = s0; tb < s1; tb += a.tch) {
       const int nt = min(a.tch, s1 - tb);
       __syncthreads();  // previous pass finished reading xs4
-      for (int idx = threadIdx.x; idx < nt * K4; idx += kThreads) {
-        const int tt = idx / K4, f = idx - tt * K4;
-        const int c = f / kQ, q = f - c * kQ;
-        float4 v;
-        if constexpr (GATEUP) {
-          const int s = tb + tt;
-          const int tok = a.identity_tokens > 0 ? s : a.sorted_pair[s] / a.top_k;
-          const uint2 raw = *reinterpret_cast<const uint2*>(a.x + static_cast<size_t>(tok) * K + 4 * f);
-          v = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
-                          __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
-        } else {
-          v = *reinterpret_cast<const float4*>(a.h + static_cast<size_t>(tb + tt) * K + 4 * f);
+      if constexpr (GATEUP && BITS == 4) {
+        // bf16 operand words + one correction per chunk (common.cuh, W4 with
+        // bf16 operands); the 4 words of a chunk sit in 4 adjacent lanes
+        const int K8 = K / 8, nw = nt * K8;
+        for (int base = 0; base < nw; base += kThreads) {
+          const int idx = base + threadIdx.x;
+          const bool ok = idx < nw;
+          const int tt = ok ? idx / K8 : 0, wi = ok ? idx - tt * K8 : 0;
+          const int c = wi >> 2, q = wi & 3;
+          float corr = 0.0f;
+          if (ok) {
+            const int s = tb + tt;
+            const int tok = a.identity_tokens > 0 ? s : a.sorted_pair[s] / a.top_k;
+            const uint4 raw = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(tok) * K + 8 * wi);
+            xq[tt * Kw + ((c / LPR) * 4 + q) * LPR + (c % LPR)] = w4_pack_x(raw, corr);
+          }
+          corr += __shfl_xor_sync(kFullMask, corr, 1);
+          corr += __shfl_xor_sync(kFullMask, corr, 2);
+          if (ok && q == 0) cq[tt * CW + c] = corr;
         }
-        const int k0 = 4 * f;
-        v.x *= act_prescale<BITS>(k0);
-        v.y *= act_prescale<BITS>(k0 + 1);
-        v.z *= act_prescale<BITS>(k0 + 2);
-        v.w *= act_prescale<BITS>(k0 + 3);
-        xs4[tt * K4p + ((c / LPR) * kQ + q) * LPR + (c % LPR)] = v;
+      } else {
+        for (int idx = threadIdx.x; idx < nt * K4; idx += kThreads) {
+          const int tt = idx / K4, f = idx - tt * K4;
+          const int c = f / kQ, q = f - c * kQ;
+          float4 v;
+          if constexpr (GATEUP) {
+            const int s = tb + tt;
+            const int tok = a.identity_tokens > 0 ? s : a.sorted_pair[s] / a.top_k;
+            const uint2 raw = *reinterpret_cast<const uint2*>(a.x + static_cast<size_t>(tok) * K + 4 * f);
+            v = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                            __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+          } else {
+            v = *reinterpret_cast<const float4*>(a.h + static_cast<size_t>(tb + tt) * K + 4 * f);
+          }
+          const int k0 = 4 * f;
+          v.x *= act_prescale<BITS>(k0);
+          v.y *= act_prescale<BITS>(k0 + 1);
+          v.z *= act_prescale<BITS>(k0 + 2);
+          v.w *= act_prescale<BITS>(k0 + 3);
+          xs4[tt * K4p + ((c / LPR) * kQ + q) * LPR + (c % LPR)] = v;
+        }
       }
       __syncthreads();
 
@@ -130,13 +156,25 @@ __global__ void __launch_bounds__(kThreads) expert_matvec_kernel(MatvecArgs a) {
               wv1 = ld_stream16(w1 + static_cast<size_t>(c) * 16);
               s1v = bf16_to_f32(__ldg(sc1 + (c * kCodes) / a.p1.group));
             }
-            const float4* xb = xs4 + (it * kQ) * LPR + sl;
+            if constexpr (GATEUP && BITS == 4) {
+              const uint4* xb = xq + (it * 4) * LPR + sl;
 #pragma unroll
-            for (int t = 0; t < kMaxTch; ++t) {
-              if (t < nt) {
-                const float4* xt = xb + t * K4p;
-                acc0[t] = fmaf(s0v, chunk_dot<BITS>(wv0, xt, LPR), acc0[t]);
-                if constexpr (GATEUP) acc1[t] = fmaf(s1v, chunk_dot<BITS>(wv1, xt, LPR), acc1[t]);
+              for (int t = 0; t < kMaxTch; ++t) {
+                if (t < nt) {
+                  const float cr = cq[t * CW + c];
+                  acc0[t] = fmaf(s0v, w4_chunk_dot_bf16(wv0, xb + t * Kw, LPR, cr), acc0[t]);
+                  acc1[t] = fmaf(s1v, w4_chunk_dot_bf16(wv1, xb + t * Kw, LPR, cr), acc1[t]);
+                }
+              }
+            } else {
+              const float4* xb = xs4 + (it * kQ) * LPR + sl;
+#pragma unroll
+              for (int t = 0; t < kMaxTch; ++t) {
+                if (t < nt) {
+                  const float4* xt = xb + t * K4p;
+                  acc0[t] = fmaf(s0v, chunk_dot<BITS>(wv0, xt, LPR), acc0[t]);
+                  if constexpr (GATEUP) acc1[t] = fmaf(s1v, chunk_dot<BITS>(wv1, xt, LPR), acc1[t]);
+                }
               }
             }
           }

@@ -66,7 +66,8 @@ struct DecodeFusedParams {
   int T, E, top_k, use_softmax, renorm;
   float* hbuf;
   uint16_t* out;
-  unsigned* bar;  // 2 words, zero-initialised grid-barrier state
+  unsigned long long* bar;  // grid-barrier arrival counter, zero-initialised, never reset
+  unsigned long long* trace;  // optional [num_sms][16] phase timestamps (ns)
   int* status;
   int num_sms;
 };

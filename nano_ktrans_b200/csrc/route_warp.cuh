@@ -5,10 +5,13 @@
 //     w = bf16(w / bf16(sum(w)))   (bf16 tensor ops: fp32 math, bf16 result)
 //   Mixtral routing: (w, ids) = topk(logits, k); w = bf16(softmax_fp32(w)).
 //
-// Each lane holds experts lane, lane+32, ...; the k picks are made by
-// repeated warp arg-max with ties broken by (value desc, expert index asc);
-// NaN ranks above every number, as in torch.topk.  Lane j < k returns the
-// j-th pick (expert id and bf16-rounded weight as fp32).
+// Ranking.  Every candidate becomes one unique 32-bit key: the high 16 bits
+// are an order-preserving image of its bf16 value (NaN mapped to the top, as
+// torch.topk ranks NaN first), the low 16 bits are 0xFFFF - expert, so equal
+// values rank by ascending expert index.  Each of the k picks is one
+// warp-wide `redux.sync.max` over the lanes' best remaining keys, instead of
+// a shuffle tree of compare-and-select steps.  Lane j < k returns the j-th
+// pick (expert id and bf16-rounded weight as fp32).
 #pragma once
 
 #include <math.h>
@@ -19,11 +22,26 @@
 
 namespace moe {
 
-MOE_DEV bool rank_before(float a, int ia, float b, int ib) {
-  const bool na = isnan(a), nb = isnan(b);
-  if (na != nb) return na;
-  if (!na && a != b) return a > b;
-  return ia < ib;
+// Monotonic map fp32 -> uint32 (a < b  <=>  key(a) < key(b) for non-NaN).
+MOE_DEV uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+MOE_DEV float order_key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Key of a bf16-valued fp32 candidate `v` for expert `e`.
+MOE_DEV uint32_t rank_key(float v, int e) {
+  const uint32_t hi = isnan(v) ? 0xffff0000u : (order_key(v) & 0xffff0000u);
+  return hi | static_cast<uint32_t>(0xffff - e);
+}
+
+// bf16 value carried by a rank key (NaN keys return a NaN).
+MOE_DEV float rank_key_value(uint32_t key) {
+  const uint32_t hi = key & 0xffff0000u;
+  return __uint_as_float((hi & 0x80000000u) ? (hi & 0x7fff0000u) : (~hi & 0xffff0000u));
 }
 
 template <int EPL>
@@ -37,12 +55,11 @@ MOE_DEV void route_token_warp(const uint16_t* __restrict__ row, int E, int top_k
     v[i] = e < E ? bf16_to_f32(row[e]) : 0.0f;
   }
   if (use_softmax) {
-    float m = -INFINITY;
+    uint32_t mk = 0;
 #pragma unroll
     for (int i = 0; i < EPL; ++i)
-      if (i * 32 + lane < E) m = fmaxf(m, v[i]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
+      if (i * 32 + lane < E) mk = max(mk, order_key(v[i]));
+    const float m = order_key_value(__reduce_max_sync(kFullMask, mk));
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
@@ -56,63 +73,45 @@ MOE_DEV void route_token_warp(const uint16_t* __restrict__ row, int E, int top_k
 #pragma unroll
     for (int i = 0; i < EPL; ++i) v[i] = round_bf16(v[i] / s);
   }
+  uint32_t key[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    key[i] = e < E ? rank_key(v[i], e) : 0u;  // valid keys are never 0
+  }
 
-  uint32_t taken = 0;
-  float my_val = 0.0f;
+  float my_val = 0.0f, sum = 0.0f, v0 = 0.0f, exsum = 0.0f;
   my_id = 0;
+#pragma unroll 1
   for (int j = 0; j < top_k; ++j) {
-    float bv = 0.0f;
-    int bi = 0x7fffffff;
+    uint32_t best = 0;
+    int bi = 0;
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
-      const int e = i * 32 + lane;
-      if (e < E && !((taken >> i) & 1u) && (bi == 0x7fffffff || rank_before(v[i], e, bv, bi))) {
-        bv = v[i];
-        bi = e;
+      if (key[i] > best) {
+        best = key[i];
+        bi = i;
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(kFullMask, bv, off);
-      const int oi = __shfl_xor_sync(kFullMask, bi, off);
-      if (oi != 0x7fffffff && (bi == 0x7fffffff || rank_before(ov, oi, bv, bi))) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const uint32_t m = __reduce_max_sync(kFullMask, best);
+    if (best == m) key[bi] = 0;  // keys are unique: exactly one lane owns the pick
+    const float val = rank_key_value(m);
     if (lane == j) {
-      my_val = bv;
-      my_id = bi;
+      my_val = val;
+      my_id = 0xffff - static_cast<int>(m & 0xffffu);
     }
+    sum += val;  // slot-order fp32 sum (a bf16 sum accumulates in fp32)
+    if (j == 0) v0 = val;
+    exsum += expf(val - v0);
   }
 
   float w = my_val;
   if (use_softmax) {
-    if (renorm) {
-      float s = 0.0f;  // sequential sum in slot order (a bf16 sum accumulates in fp32)
-      for (int j = 0; j < top_k; ++j) s += __shfl_sync(kFullMask, my_val, j);
-      w = my_val / round_bf16(s);
-    }
+    if (renorm) w = my_val / round_bf16(sum);
   } else {
-    const float m = __shfl_sync(kFullMask, my_val, 0);
-    const float ex = lane < top_k ? expf(my_val - m) : 0.0f;
-    float s = 0.0f;
-    for (int j = 0; j < top_k; ++j) s += __shfl_sync(kFullMask, ex, j);
-    w = ex / s;
+    w = expf(my_val - v0) / exsum;
   }
   my_w = round_bf16(w);
-}
-
-// Dispatch on experts-per-lane.  F is called as F(integral_constant<EPL>).
-template <typename F>
-MOE_DEV void with_epl(int E, F&& f) {
-  if (E <= 32) f(std::integral_constant<int, 1>{});
-  else if (E <= 64) f(std::integral_constant<int, 2>{});
-  else if (E <= 128) f(std::integral_constant<int, 4>{});
-  else if (E <= 256) f(std::integral_constant<int, 8>{});
-  else if (E <= 512) f(std::integral_constant<int, 16>{});
-  else f(std::integral_constant<int, 32>{});
 }
 
 }  // namespace moe

@@ -151,6 +151,21 @@ class MoeLayer:
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_DECODE_FUSED, int(bool(enabled))), self._h,
                    "moe_set_option")
 
+    def set_trace(self, enabled: bool) -> None:
+        """Record per-CTA phase timestamps in the single-launch decode kernel."""
+        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_TRACE, int(bool(enabled))), self._h, "moe_set_option")
+
+    def read_trace(self, stream=None):
+        """[num_ctas][6] phase timestamps (ns) of the last traced decode launch:
+        entry, routing done, gate/up done, grid barrier passed, h staged, exit."""
+        import numpy as np
+
+        buf = (ctypes.c_uint64 * (1024 * 16))()
+        n = ctypes.c_int32(0)
+        _lib.check(_lib.lib().moe_read_trace(self._h, buf, len(buf), ctypes.byref(n), _stream_handle(stream)),
+                   self._h, "moe_read_trace")
+        return np.frombuffer(buf, dtype=np.uint64)[: n.value * 16].reshape(n.value, 16).copy()
+
     def profile_begin(self, kernel_class: int, max_samples: int) -> None:
         _lib.check(_lib.lib().moe_profile_begin(self._h, kernel_class, max_samples), self._h, "moe_profile_begin")
 
