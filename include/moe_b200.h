@@ -191,6 +191,31 @@ int moe_profile_end(void* handle, float* total_ms, int32_t* samples);
 int moe_last_error(void* handle, char* buf, size_t len);
 void moe_destroy(void* handle);
 
+/* Single-launch decode step (route + experts + combine, as moe_forward)
+ * that allocates nothing: no handle, no cudaMalloc/cudaFree.  For callers
+ * that cannot allocate device memory when they run a layer (a memory budget
+ * fixed up front, an embedding that only hands out pre-registered buffers, a
+ * caller that must not enter the allocator while other work is in flight).
+ * No counterpart in the reference.
+ *   - The caller passes the layer description, the device weight pointers
+ *     (layout as for moe_set_weights), x [T, H] and logits [T, E] (bf16), and
+ *     the outputs out [T, H] (bf16), topk_ids [T, k] (int64), topk_weights
+ *     [T, k] (bf16); status_dev (nullable) receives the device status bits
+ *     (see moe_read_status).
+ *   - Scratch is one file-scope device array per GPU that loads the library:
+ *     T * top_k * inter_size must be <= 65536 floats, and the batch must fit
+ *     the single-launch kernel (T <= 4, T * top_k <= 32, E <= 256); larger
+ *     calls return MOE_ERANGE with a message and launch nothing.
+ *   - Every call on a device shares that array: calls whose kernels overlap
+ *     on the GPU race and give wrong results; serialise them.
+ *   - The first call on a device looks up the array's address
+ *     (cudaGetSymbolAddress); make it outside any stream capture.
+ * err/err_len receive a message on failure. */
+int moe_decode_noalloc(const moe_layer_desc* desc, const moe_weights* w, const uint16_t* x_dev,
+                       const uint16_t* logits_dev, int32_t num_tokens, uint16_t* out_dev,
+                       int64_t* topk_ids_dev, uint16_t* topk_weights_dev, int32_t* status_dev,
+                       void* stream, char* err, size_t err_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -59,6 +59,8 @@ SIGNATURES = {
     "moe_profile_end": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_i32)]),
     "moe_last_error": (_i32, [_vp, _cp, _sz]),
     "moe_destroy": (None, [_vp]),
+    "moe_decode_noalloc": (_i32, [ctypes.POINTER(MoeLayerDesc), ctypes.POINTER(MoeWeights), _vp, _vp, _i32, _vp, _vp,
+                                  _vp, _vp, _vp, _cp, _sz]),
 }
 
 _lib = None
