@@ -165,7 +165,14 @@ enum moe_option {
   MOE_OPT_DECODE_FUSED = 1,
   /* 1: the single-launch decode kernel records per-CTA phase timestamps
    * (allocates num_SMs * 8 * 8 bytes); read them with moe_read_trace. */
-  MOE_OPT_TRACE = 2
+  MOE_OPT_TRACE = 2,
+  /* Expert projections of the multi-kernel path: 0 = matvec kernels only;
+   * 1 (default) = tensor-core grouped GEMM once T * top_k >= 4 * num_experts;
+   * 2 = grouped GEMM for every batch the single-launch kernel does not take.
+   * The GEMM path needs inter and hidden multiples of 128 and, for W4,
+   * group_size a multiple of 64 (W8: per-channel); value 2 on another shape
+   * is refused. */
+  MOE_OPT_GEMM = 3
 };
 
 /* Copy the phase timestamps of the last traced single-launch decode step:

@@ -42,6 +42,15 @@ struct Handle {
   unsigned long long* grid_bar = nullptr;  // grid-barrier arrival counter of the fused decode kernel
   bool decode_fused = true;
   unsigned long long* trace = nullptr;  // [num_sms][16] phase timestamps when tracing
+  // prefill GEMM path: tensor maps over the activation buffers and the codes
+  int32_t* tile_off = nullptr;  // [E+1]
+  int gemm_mode = 1;            // 0 never, 1 by batch size, 2 whenever the shape allows
+  bool gemm_maps = false;       // tensor maps encoded (shape supported, driver entry point found)
+  alignas(64) unsigned char tm_x[128];     // fp16 [max_pairs][H] over ybuf (x packed in pair order)
+  alignas(64) unsigned char tm_h[128];     // fp16 [max_pairs][I] over hbuf (SiLU(g)*u)
+  alignas(64) unsigned char tm_gate[128];  // uint8 [E*I][H*bits/8]
+  alignas(64) unsigned char tm_up[128];
+  alignas(64) unsigned char tm_down[128];  // uint8 [E*H][I*bits/8]
   std::string err;
   int last_launches = 0;
   // profiling: events bracketing one kernel class
@@ -123,6 +132,38 @@ const char* validate_desc(const moe_layer_desc& d) {
 
 size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
+// Tensor maps of the prefill GEMM path.  The activation maps cover the
+// workspace buffers at their full max_pairs extent: x (fp16) aliases ybuf,
+// which the down GEMM writes only after the gate/up GEMM has read x, and
+// SiLU(g)*u (fp16) aliases hbuf.  False when a projection's shape is outside
+// the GEMM rules; the multi-kernel matvec path then serves every batch.
+bool encode_gemm_maps(Handle* h) {
+  const moe_layer_desc& d = h->d;
+  const int H = d.hidden_size, I = d.inter_size, E = d.num_experts, bits = d.bits;
+  const uint64_t P = static_cast<uint64_t>(d.max_tokens) * d.top_k;
+  const QuantProj gate = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H);
+  const QuantProj down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
+  if (!moe::gemm_shape_ok(bits, gate) || !moe::gemm_shape_ok(bits, down)) return false;
+  const uint32_t code_box = moe::kGemmBK * bits / 8;
+  bool ok = moe::make_tmap_2d(h->tm_x, h->ybuf, true, H, P, moe::kGemmBK, moe::kGemmBN, true);
+  ok = ok && moe::make_tmap_2d(h->tm_h, h->hbuf, true, I, P, moe::kGemmBK, moe::kGemmBN, true);
+  ok = ok && moe::make_tmap_2d(h->tm_gate, h->w.gate_q_dev, false, static_cast<uint64_t>(H) * bits / 8,
+                               static_cast<uint64_t>(E) * I, code_box, moe::kGemmBM, false);
+  ok = ok && moe::make_tmap_2d(h->tm_up, h->w.up_q_dev, false, static_cast<uint64_t>(H) * bits / 8,
+                               static_cast<uint64_t>(E) * I, code_box, moe::kGemmBM, false);
+  ok = ok && moe::make_tmap_2d(h->tm_down, h->w.down_q_dev, false, static_cast<uint64_t>(I) * bits / 8,
+                               static_cast<uint64_t>(E) * H, code_box, moe::kGemmBM, false);
+  return ok;
+}
+
+// The GEMM path pays off once experts see several tokens each; below that
+// the matvec kernels stream the same weight bytes with less fixed cost.
+bool use_gemm(const Handle* h, int T) {
+  if (!h->gemm_maps || h->gemm_mode == 0) return false;
+  if (h->gemm_mode == 2) return true;
+  return static_cast<int64_t>(T) * h->d.top_k >= 4LL * h->d.num_experts;
+}
+
 }  // namespace
 
 extern "C" {
@@ -154,7 +195,8 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   const size_t o_status = take(4), o_counts = take(4 * E), o_offsets = take(4 * (E + 1)), o_active = take(4 * E),
                o_nact = take(4), o_sorted = take(4 * P), o_pos = take(4 * P), o_h = take(4 * P * I),
                o_y = take(4 * P * H), o_shh = take(S ? 4 * T * S : 0), o_shy = take(S ? 4 * T * H : 0),
-               o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P), o_bar = take(8);
+               o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P), o_bar = take(8),
+               o_tiles = take(4 * (E + 1));
   h->ws_bytes = off;
   cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
   if (e != cudaSuccess) {
@@ -180,6 +222,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   h->ids_tmp = reinterpret_cast<int64_t*>(b + o_ids);
   h->w_tmp = reinterpret_cast<uint16_t*>(b + o_w);
   h->grid_bar = reinterpret_cast<unsigned long long*>(b + o_bar);
+  h->tile_off = reinterpret_cast<int32_t*>(b + o_tiles);
   e = cudaMemset(h->ws, 0, h->ws_bytes);
   if (e != cudaSuccess) {
     fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
@@ -220,6 +263,7 @@ int moe_set_weights(void* handle, const moe_weights* w, char* err, size_t err_le
   }
   h->w = *w;
   h->has_weights = true;
+  h->gemm_maps = encode_gemm_maps(h);
   return MOE_OK;
 }
 
@@ -292,12 +336,48 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
   const QuantProj gate = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H);
   const QuantProj up = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H);
   const QuantProj down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
-  prof_mark(h, MOE_K_GATEUP, false, st);
-  launches += moe::launch_gateup(d.bits, x, h->rt, k, max_active, T, 0, gate, up, h->hbuf, h->num_sms, st);
-  prof_mark(h, MOE_K_GATEUP, true, st);
-  prof_mark(h, MOE_K_DOWN, false, st);
-  launches += moe::launch_down(d.bits, h->hbuf, h->rt, max_active, T, 0, down, h->ybuf, h->num_sms, st);
-  prof_mark(h, MOE_K_DOWN, true, st);
+  if (h->gemm_mode == 2 && !h->gemm_maps)
+    return fail(h, MOE_EINVAL, "GEMM path forced but this layer's shape is outside its rules");
+  if (use_gemm(h, T)) {
+    moe::launch_tile_table(h->rt, h->tile_off, st);
+    moe::launch_pack_x(d.bits, x, h->rt, E, k, 0, H, T * k, h->ybuf, h->num_sms, st);
+    launches += 2;
+    moe::GemmLaunch g{};
+    g.rt = h->rt;
+    g.tile_off = h->tile_off;
+    g.status = h->rt.status;
+    g.max_pairs = T * k;
+    g.max_active = max_active;
+    g.p0 = gate;
+    g.p1 = up;
+    g.tmap_x = h->tm_x;
+    g.tmap_w0 = h->tm_gate;
+    g.tmap_w1 = h->tm_up;
+    g.hout = h->hbuf;
+    prof_mark(h, MOE_K_GATEUP, false, st);
+    int rc = moe::launch_grouped_gemm(d.bits, true, g, st);
+    prof_mark(h, MOE_K_GATEUP, true, st);
+    if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (gate/up): shared-memory opt-in refused");
+    g.p0 = down;
+    g.p1 = down;
+    g.tmap_x = h->tm_h;
+    g.tmap_w0 = h->tm_down;
+    g.tmap_w1 = h->tm_down;
+    g.hout = nullptr;
+    g.yout = h->ybuf;
+    prof_mark(h, MOE_K_DOWN, false, st);
+    rc = moe::launch_grouped_gemm(d.bits, false, g, st);
+    prof_mark(h, MOE_K_DOWN, true, st);
+    if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (down): shared-memory opt-in refused");
+    launches += 2;
+  } else {
+    prof_mark(h, MOE_K_GATEUP, false, st);
+    launches += moe::launch_gateup(d.bits, x, h->rt, k, max_active, T, 0, gate, up, h->hbuf, h->num_sms, st);
+    prof_mark(h, MOE_K_GATEUP, true, st);
+    prof_mark(h, MOE_K_DOWN, false, st);
+    launches += moe::launch_down(d.bits, h->hbuf, h->rt, max_active, T, 0, down, h->ybuf, h->num_sms, st);
+    prof_mark(h, MOE_K_DOWN, true, st);
+  }
   const float* sg = nullptr;
   const float* sy = nullptr;
   if (add_shared && d.shared_inter > 0) {
@@ -407,6 +487,12 @@ int moe_set_option(void* handle, int32_t option, int32_t value) {
   if (h == nullptr) return MOE_EINVAL;
   switch (option) {
     case MOE_OPT_DECODE_FUSED: h->decode_fused = value != 0; return MOE_OK;
+    case MOE_OPT_GEMM:
+      if (value < 0 || value > 2) return fail(h, MOE_EINVAL, "moe_set_option(gemm): value must be 0, 1 or 2");
+      if (value == 2 && h->has_weights && !h->gemm_maps)
+        return fail(h, MOE_EINVAL, "moe_set_option(gemm): this layer's shape is outside the GEMM path's rules");
+      h->gemm_mode = value;
+      return MOE_OK;
     case MOE_OPT_TRACE:
       if (value && h->trace == nullptr) {
         const size_t bytes = static_cast<size_t>(h->num_sms) * 16 * sizeof(unsigned long long);

@@ -1,0 +1,527 @@
+// grouped_gemm.cu — prefill path: per-expert grouped GEMM on tcgen05 tensor
+// cores with the weights dequantized in shared memory.
+//
+// Replaces, for batches with many tokens per expert, the per-expert loop of
+// nano_ktrans/kernels/cpu_moe.py:515-536 (gate/up/down via the grouped W4A32
+// matvec, quantized_ops.py:86-124, SiLU(gate)*up at cpu_moe.py:448).
+//
+// Orientation ("swap AB"): the MMA's M = 128 weight rows (output features),
+// N = 128 tokens of one expert, K = the reduction dimension in steps of 64.
+//   A  (weights)     fp16, dequantized by CUDA cores from the W4/W8 codes into
+//                    a 128 x 64 K-major tile with the 128-byte swizzle;
+//   B  (activations) fp16 [pairs, K] in expert-sorted pair order, loaded by
+//                    TMA (tensor map, 128-byte swizzle);
+//   D               fp32 in tensor memory (TMEM).
+// Exactness: (q - z) * s has at most 3+8 (W4) significant bits, so it is
+// exact in fp16; W8 per-channel uses (q - 128) (exact) and applies the scale
+// in the epilogue.  Activations are bf16 inputs converted to fp16 (exact for
+// magnitudes in [2^-14, 65504]) and the SiLU*up intermediate is rounded to
+// fp16 once.  Products are exact, accumulation is fp32.
+//
+// K order: the dequant writes each word's codes in the order its nibble /
+// byte extraction produces them (W4: 0,4,1,5,2,6,3,7 within each 8 codes;
+// W8: 0,2,1,3 within each 4).  A GEMM is unchanged by a permutation of K
+// applied to both operands, so the activation buffers are written in that
+// same order (pack_x_kernel, and the gate/up epilogue for the down GEMM).
+//
+// CTA roles (192 threads): warp 0 issues the TMA loads; warp 1 owns TMEM and
+// one lane issues the MMAs; warps 2-5 (128 threads, thread = weight row)
+// dequantize, then run the epilogue from TMEM.  Stages are handed over with
+// mbarriers; every wait is bounded and records kStatusTimeout on expiry.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moe {
+namespace gg {
+
+constexpr int BM = kGemmBM;  // weight rows per tile
+constexpr int BN = kGemmBN;  // tokens per tile
+constexpr int BK = kGemmBK;  // K per stage (one 128-byte fp16 row)
+constexpr int kThreads = 192;
+constexpr uint32_t kSpin = 1u << 22;  // bounded waits: the kernel records kStatusTimeout and unwinds
+
+MOE_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+MOE_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+MOE_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+MOE_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+MOE_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpin; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+// 2-D tiled TMA load, global -> this CTA's shared memory (no multicast).
+MOE_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// K-major operand tile with the 128-byte swizzle: rows of 128 bytes, 8-row
+// groups 1024 bytes apart (stride byte offset), descriptor version 1.
+MOE_DEV uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (unused when swizzled)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;                 // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: D f32, A f16, B f16, both K-major, M x N.
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+
+MOE_DEV void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+MOE_DEV void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes.
+MOE_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Position, within its group of 8, at which code/feature j of that group is
+// stored in the K-permuted activation layout.
+template <int BITS>
+MOE_DEV int kpos(int j) {
+  if constexpr (BITS == 4) {
+    return (j & 3) * 2 + (j >> 2);  // codes 0,4,1,5,2,6,3,7 -> j = 0..7 at 0,2,4,6,1,3,5,7
+  } else {
+    return (j & 4) + ((j & 1) << 1) + ((j >> 1) & 1);  // 0,2,1,3 within each 4
+  }
+}
+
+// Dequantize 16 bytes of codes (32 W4 or 16 W8 codes) of one row into fp16
+// in storage order; `sc` is the row's fp16 scale (ignored for W8).
+template <int BITS>
+MOE_DEV void dequant16(uint4 c, __half2 sc, uint4* out) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+  if constexpr (BITS == 4) {
+    const __half2 bias = __float2half2_rn(1032.0f);  // 1024 + 8
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t v[4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const uint32_t m = ((w[q] >> (4 * s)) & 0x000F000Fu) | 0x64006400u;  // fp16 (1024 + q_s, 1024 + q_{s+4})
+        __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&m), bias);    // q - 8, exact
+        h = __hmul2(h, sc);                                                  // (q - 8) * s, exact
+        v[s] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      out[q] = make_uint4(v[0], v[1], v[2], v[3]);
+    }
+  } else {
+    const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
+    uint32_t v[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t m02 = __byte_perm(w[q], 0x64646464u, 0x4240);  // fp16 (1024 + b0, 1024 + b2)
+      const uint32_t m13 = __byte_perm(w[q], 0x64646464u, 0x4341);  // fp16 (1024 + b1, 1024 + b3)
+      __half2 h0 = __hsub2(*reinterpret_cast<const __half2*>(&m02), bias);
+      __half2 h1 = __hsub2(*reinterpret_cast<const __half2*>(&m13), bias);
+      v[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
+      v[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
+    }
+    out[0] = make_uint4(v[0], v[1], v[2], v[3]);
+    out[1] = make_uint4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+struct GemmArgs {
+  const int32_t* offsets;   // [E+1]
+  const int32_t* active;    // [E]
+  const int32_t* n_active;  // [1]
+  const int32_t* tile_off;  // [E+1] token-tile prefix over active experts
+  const uint16_t* s0;       // scales of projection 0 (gate or down)
+  const uint16_t* s1;       // scales of projection 1 (up)
+  int sstride, group;
+  int N, K;                 // rows per expert, reduction dim
+  __half* hout;             // gate/up: SiLU*up [pairs][N] (K-permuted within 8)
+  float* yout;              // down: y [pairs][N]
+  int* status;
+};
+
+template <int BITS, bool GATEUP>
+struct Smem {
+  static constexpr int kCodeRow = BK * BITS / 8;  // code bytes per row per stage
+  static constexpr int kX = BN * 128;             // activation tile
+  static constexpr int kA = BM * 128;             // dequantized weight tile
+  static constexpr int kC = BM * kCodeRow;        // code tile
+  static constexpr int kNP = GATEUP ? 2 : 1;
+  static constexpr int kStage = kX + kNP * (kA + kC);
+  static constexpr int kStages = GATEUP ? 3 : 4;
+  static constexpr int kBarOff = kStages * kStage;
+  static constexpr int kBytes = kBarOff + 256 + 1024;  // barriers + TMEM slot + alignment slack
+};
+
+template <int BITS, bool GATEUP>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w0,
+                        const __grid_constant__ CUtensorMap tm_w1, GemmArgs a) {
+  using L = Smem<BITS, GATEUP>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- tile -> (expert, token tile, feature block) ----
+  const int nfb = a.N / BM;
+  const int fb = blockIdx.x % nfb, tt = blockIdx.x / nfb;
+  const int n_act = *a.n_active;
+  if (tt >= a.tile_off[n_act]) return;  // CTA-uniform, before any barrier
+  int lo = 0, hi = n_act;               // tile_off[lo] <= tt < tile_off[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (a.tile_off[mid] <= tt) lo = mid;
+    else hi = mid;
+  }
+  const int e = a.active[lo];
+  const int s_begin = a.offsets[e] + (tt - a.tile_off[lo]) * BN;
+  const int ntok = min(BN, a.offsets[e + 1] - s_begin);
+  const int wrow = e * a.N + fb * BM;  // first weight row (codes tensor row)
+  const int nk = a.K / BK;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  // full[s] = bars[s], afull[s] = bars[kStages + s], empty[s] = bars[2*kStages + s], acc = bars[3*kStages]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBarOff + 8 * (3 * L::kStages + 1));
+  __shared__ int abort_flag_s;
+  volatile int* abort_flag = &abort_flag_s;  // set by whichever role times out first
+
+  if (tid == 0) {
+    for (int s = 0; s < L::kStages; ++s) {
+      mbar_init(smem_u32(&bars[s]), 1);
+      mbar_init(smem_u32(&bars[L::kStages + s]), 128);
+      mbar_init(smem_u32(&bars[2 * L::kStages + s]), 1);
+    }
+    mbar_init(smem_u32(&bars[3 * L::kStages]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    *abort_flag = 0;
+  }
+  if (warp == 1) {  // TMEM: kNP accumulators of BN fp32 columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(L::kNP * BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  auto give_up = [&]() {
+    if (!*abort_flag) {
+      *abort_flag = 1;
+      atomicOr(a.status, kStatusTimeout);
+    }
+  };
+  auto stage_ptr = [&](int s) { return smem + s * L::kStage; };
+  // stage layout: X | A0 | C0 | A1 | C1
+  auto x_tile = [&](int s) { return stage_ptr(s); };
+  auto a_tile = [&](int s, int p) { return stage_ptr(s) + L::kX + p * (L::kA + L::kC); };
+  auto c_tile = [&](int s, int p) { return stage_ptr(s) + L::kX + p * (L::kA + L::kC) + L::kA; };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int c = 0; c < nk && !*abort_flag; ++c) {
+        const int s = c % L::kStages;
+        if (c >= L::kStages &&
+            !mbar_wait(smem_u32(&bars[2 * L::kStages + s]), static_cast<uint32_t>(((c / L::kStages) - 1) & 1))) {
+          give_up();
+          break;
+        }
+        const uint32_t full = smem_u32(&bars[s]);
+        mbar_expect_tx(full, static_cast<uint32_t>(L::kX + L::kNP * L::kC));
+        tma_load_2d(smem_u32(x_tile(s)), &tm_x, c * BK, s_begin, full);
+        tma_load_2d(smem_u32(c_tile(s, 0)), &tm_w0, c * L::kCodeRow, wrow, full);
+        if constexpr (GATEUP) tma_load_2d(smem_u32(c_tile(s, 1)), &tm_w1, c * L::kCodeRow, wrow, full);
+        issued = c + 1;
+      }
+      if (*abort_flag) {
+        // no copy may still be landing in shared memory when the CTA exits
+        for (int c = max(0, issued - L::kStages); c < issued; ++c)
+          mbar_wait(smem_u32(&bars[c % L::kStages]), static_cast<uint32_t>((c / L::kStages) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      for (int c = 0; c < nk && !*abort_flag; ++c) {
+        const int s = c % L::kStages;
+        const uint32_t par = static_cast<uint32_t>((c / L::kStages) & 1);
+        if (!mbar_wait(smem_u32(&bars[L::kStages + s]), par) || !mbar_wait(smem_u32(&bars[s]), par)) {
+          give_up();
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t db = sw128_desc(smem_u32(x_tile(s)));
+        const uint64_t da0 = sw128_desc(smem_u32(a_tile(s, 0)));
+        const uint64_t da1 = GATEUP ? sw128_desc(smem_u32(a_tile(s, 1))) : 0;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
+          umma_f16(tmem, da0 + 2 * kk, db + 2 * kk, acc);  // +32 bytes per K step of 16
+          if constexpr (GATEUP) umma_f16(tmem + BN, da1 + 2 * kk, db + 2 * kk, acc);
+        }
+        umma_commit(smem_u32(&bars[2 * L::kStages + s]));
+      }
+      umma_commit(smem_u32(&bars[3 * L::kStages]));
+      // every MMA has finished (normal or aborted) before TMEM is released
+      if (!mbar_wait(smem_u32(&bars[3 * L::kStages]), 0u)) give_up();
+    }
+  } else {
+    // ---------------- dequant (warps 2-5), then epilogue ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;
+    const size_t srow = static_cast<size_t>(wrow + r) * a.sstride;
+    for (int c = 0; c < nk; ++c) {
+      const int s = c % L::kStages;
+      if (*abort_flag) break;
+      if (!mbar_wait(smem_u32(&bars[s]), static_cast<uint32_t>((c / L::kStages) & 1))) {
+        give_up();
+        break;
+      }
+#pragma unroll
+      for (int p = 0; p < L::kNP; ++p) {
+        __half2 sc = __float2half2_rn(1.0f);
+        if constexpr (BITS == 4) {
+          const uint16_t* sp = p == 0 ? a.s0 : a.s1;
+          sc = __float2half2_rn(bf16_to_f32(__ldg(sp + srow + (c * BK) / a.group)));
+        }
+        const uint4* codes = reinterpret_cast<const uint4*>(c_tile(s, p) + r * L::kCodeRow);
+        unsigned char* arow = a_tile(s, p) + r * 128;
+#pragma unroll
+        for (int j = 0; j < L::kCodeRow / 16; ++j) {
+          uint4 o[BITS == 4 ? 4 : 2];
+          dequant16<BITS>(codes[j], sc, o);
+#pragma unroll
+          for (int q = 0; q < (BITS == 4 ? 4 : 2); ++q) {
+            const int chunk = j * (BITS == 4 ? 4 : 2) + q;  // 16-byte chunk of the 128-byte row
+            *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = o[q];
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+      mbar_arrive(smem_u32(&bars[L::kStages + s]));
+    }
+    // epilogue
+    bool ok = !*abort_flag;
+    if (ok && !mbar_wait(smem_u32(&bars[3 * L::kStages]), 0u)) {
+      give_up();
+      ok = false;
+    }
+    if (ok && !*abort_flag) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t tl = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int row = fb * BM + r;  // feature row within the expert
+      float s0w = 1.0f, s1w = 1.0f;
+      if constexpr (BITS == 8) {
+        s0w = bf16_to_f32(__ldg(a.s0 + srow));
+        if constexpr (GATEUP) s1w = bf16_to_f32(__ldg(a.s1 + srow));
+      }
+      const int col = GATEUP ? (row & ~7) + kpos<BITS>(row & 7) : row;
+      for (int j = 0; j < BN / 16; ++j) {
+        float d0[16], d1[16];
+        tmem_ld16(tl + j * 16, d0);
+        if constexpr (GATEUP) tmem_ld16(tl + BN + j * 16, d1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int n = j * 16 + i;
+          if (n < ntok) {
+            const size_t o = static_cast<size_t>(s_begin + n) * a.N + col;
+            if constexpr (GATEUP) {
+              a.hout[o] = __float2half_rn(silu_f32(d0[i] * s0w) * (d1[i] * s1w));
+            } else {
+              a.yout[o] = d0[i] * s0w;
+            }
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::kNP * BN));
+  }
+}
+
+// Token-tile prefix over the active experts: tile_off[a] = sum_{a' < a} ceil(count / BN).
+__global__ void tile_table_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+                                  const int32_t* __restrict__ n_active, int32_t* __restrict__ tile_off) {
+  if (threadIdx.x != 0) return;
+  const int n = *n_active;
+  int acc = 0;
+  for (int i = 0; i < n; ++i) {
+    tile_off[i] = acc;
+    const int e = active[i];
+    acc += (offsets[e + 1] - offsets[e] + BN - 1) / BN;
+  }
+  tile_off[n] = acc;
+}
+
+// X16[s][k'] = fp16(x[token(s)][k]) with k permuted within each group of 8 (kpos).
+template <int BITS>
+__global__ void pack_x_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ sorted_pair,
+                              const int32_t* __restrict__ offsets, int E, int top_k, int identity_tokens, int H,
+                              __half* __restrict__ x16) {
+  const int P = identity_tokens > 0 ? identity_tokens : offsets[E];
+  const int groups = H / 8;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < P * groups; idx += gridDim.x * blockDim.x) {
+    const int s = idx / groups, g = idx - s * groups;
+    const int tok = identity_tokens > 0 ? s : sorted_pair[s] / top_k;
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(tok) * H + 8 * g);
+    const uint16_t v[8] = {static_cast<uint16_t>(raw.x & 0xffff), static_cast<uint16_t>(raw.x >> 16),
+                           static_cast<uint16_t>(raw.y & 0xffff), static_cast<uint16_t>(raw.y >> 16),
+                           static_cast<uint16_t>(raw.z & 0xffff), static_cast<uint16_t>(raw.z >> 16),
+                           static_cast<uint16_t>(raw.w & 0xffff), static_cast<uint16_t>(raw.w >> 16)};
+    __half o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[kpos<BITS>(j)] = __float2half_rn(bf16_to_f32(v[j]));
+    *reinterpret_cast<uint4*>(x16 + static_cast<size_t>(s) * H + 8 * g) = *reinterpret_cast<uint4*>(o);
+  }
+}
+
+}  // namespace gg
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool make_tmap_2d(void* out_map, const void* base, bool fp16, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                  uint32_t box_rows, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const uint64_t esize = fp16 ? 2 : 1;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * esize};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      fn(reinterpret_cast<CUtensorMap*>(out_map), fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+         2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool gemm_shape_ok(int bits, const QuantProj& p) {
+  if (bits != 4 && bits != 8) return false;
+  if (p.n % gg::BM || p.k % gg::BK) return false;
+  if (bits == 4 && p.group % gg::BK) return false;  // a 64-wide K step must stay inside one scale group
+  if (bits == 8 && p.group != p.k) return false;    // W8: per-channel scale applied in the epilogue
+  return true;
+}
+
+void launch_tile_table(const RouteTables& rt, int32_t* tile_off, cudaStream_t st) {
+  gg::tile_table_kernel<<<1, 32, 0, st>>>(rt.offsets, rt.active, rt.n_active, tile_off);
+}
+
+void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, int top_k, int identity_tokens, int H,
+                   int max_pairs, void* x16, int num_sms, cudaStream_t st) {
+  const int work = max_pairs * (H / 8);
+  const int grid = std::max(1, std::min((work + 255) / 256, num_sms * 8));
+  if (bits == 4)
+    gg::pack_x_kernel<4><<<grid, 256, 0, st>>>(x, rt.sorted_pair, rt.offsets, E, top_k, identity_tokens, H,
+                                                static_cast<__half*>(x16));
+  else
+    gg::pack_x_kernel<8><<<grid, 256, 0, st>>>(x, rt.sorted_pair, rt.offsets, E, top_k, identity_tokens, H,
+                                                static_cast<__half*>(x16));
+}
+
+template <int BITS, bool GATEUP>
+static int launch_gemm_t(const GemmLaunch& g, cudaStream_t st) {
+  using L = gg::Smem<BITS, GATEUP>;
+  auto kern = gg::grouped_gemm_kernel<BITS, GATEUP>;
+  static int configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1 << (dev & 31)))) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes) != cudaSuccess) return -1;
+    configured |= 1 << (dev & 31);
+  }
+  gg::GemmArgs a{};
+  a.offsets = g.rt.offsets;
+  a.active = g.rt.active;
+  a.n_active = g.rt.n_active;
+  a.tile_off = g.tile_off;
+  a.s0 = g.p0.s;
+  a.s1 = GATEUP ? g.p1.s : nullptr;
+  a.sstride = g.p0.sstride;
+  a.group = g.p0.group;
+  a.N = g.p0.n;
+  a.K = g.p0.k;
+  a.hout = static_cast<__half*>(g.hout);
+  a.yout = g.yout;
+  a.status = g.status;
+  const int max_tiles = (g.max_pairs + gg::BN - 1) / gg::BN + g.max_active;
+  const int grid = max_tiles * (g.p0.n / gg::BM);
+  const CUtensorMap* tx = reinterpret_cast<const CUtensorMap*>(g.tmap_x);
+  const CUtensorMap* t0 = reinterpret_cast<const CUtensorMap*>(g.tmap_w0);
+  const CUtensorMap* t1 = reinterpret_cast<const CUtensorMap*>(GATEUP ? g.tmap_w1 : g.tmap_w0);
+  kern<<<grid, gg::kThreads, L::kBytes, st>>>(*tx, *t0, *t1, a);
+  return 1;
+}
+
+int launch_grouped_gemm(int bits, bool gateup, const GemmLaunch& g, cudaStream_t st) {
+  if (bits == 4) return gateup ? launch_gemm_t<4, true>(g, st) : launch_gemm_t<4, false>(g, st);
+  return gateup ? launch_gemm_t<8, true>(g, st) : launch_gemm_t<8, false>(g, st);
+}
+
+}  // namespace moe

@@ -79,4 +79,37 @@ int launch_decode_fused(int bits, const DecodeFusedParams& p, cudaStream_t st);
 void launch_dequant_rows(int bits, const QuantProj& p, int expert, int row0, int nrows, float* out,
                          cudaStream_t st);
 
+// ---- prefill path: tcgen05 grouped GEMM (grouped_gemm.cu) ----
+
+// 2-D tensor map (CUtensorMap, 128 bytes, 64-byte aligned storage at out_map)
+// over a row-major [rows][inner] fp16 or uint8 array; false if the driver
+// entry point is unavailable or the encode fails.
+bool make_tmap_2d(void* out_map, const void* base, bool fp16, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                  uint32_t box_rows, bool swizzle128);
+// Shape rules of the GEMM path for one projection (N % 128, K % 64, W4 group
+// % 64, W8 per-channel).
+bool gemm_shape_ok(int bits, const QuantProj& p);
+// Box sizes the tensor maps must be encoded with.
+constexpr int kGemmBM = 128, kGemmBN = 128, kGemmBK = 64;
+
+struct GemmLaunch {
+  RouteTables rt;
+  const int32_t* tile_off;  // [E+1] from launch_tile_table
+  QuantProj p0, p1;         // gate, up (gate/up GEMM) or down, unused
+  const void* tmap_x;       // activations fp16 [rows][K], box {64, 128}, 128-byte swizzle
+  const void* tmap_w0;      // codes of p0 as uint8 [E*N][K*bits/8], box {64*bits/8, 128}
+  const void* tmap_w1;      // codes of p1 (gate/up only)
+  void* hout;               // gate/up: fp16 SiLU(g)*u [pairs][N], K-permuted for the down GEMM
+  float* yout;              // down: fp32 [pairs][N]
+  int* status;
+  int max_pairs;            // upper bound of the pair count of this call
+  int max_active;           // upper bound of the active expert count of this call
+};
+void launch_tile_table(const RouteTables& rt, int32_t* tile_off, cudaStream_t st);
+// x16[s] = fp16(x[token of sorted pair s]) with K permuted to the dequant order.
+void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, int top_k, int identity_tokens, int H,
+                   int max_pairs, void* x16, int num_sms, cudaStream_t st);
+// 1 = launched, negative = refused (shared-memory opt-in failed).
+int launch_grouped_gemm(int bits, bool gateup, const GemmLaunch& g, cudaStream_t st);
+
 }  // namespace moe

@@ -151,6 +151,11 @@ class MoeLayer:
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_DECODE_FUSED, int(bool(enabled))), self._h,
                    "moe_set_option")
 
+    def set_gemm(self, mode: int) -> None:
+        """Expert projections of the multi-kernel path: 0 matvec only, 1 tensor-core
+        grouped GEMM for large batches (default), 2 grouped GEMM for every batch."""
+        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_GEMM, int(mode)), self._h, "moe_set_option")
+
     def set_trace(self, enabled: bool) -> None:
         """Record per-CTA phase timestamps in the single-launch decode kernel."""
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_TRACE, int(bool(enabled))), self._h, "moe_set_option")

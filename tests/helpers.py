@@ -100,3 +100,19 @@ def assert_parity(out_bf16_bits: np.ndarray, ref_f32: np.ndarray, max_abs: float
     assert err.max() <= max_abs, f"max-abs {err.max():.3e} > {max_abs}"
     assert err.mean() / denom <= mean_rel, f"mean-rel {err.mean() / denom:.3e} > {mean_rel}"
     return float(err.max()), float(err.mean() / denom)
+
+
+def assert_paths_agree(a_bf16_bits: np.ndarray, b_bf16_bits: np.ndarray, max_abs: float = 2e-2,
+                       mean_rel: float = 5e-3):
+    """Two device paths, each rounded to bf16 once, agree: |a - b| within the
+    absolute bar plus one bf16 unit in the last place of b (each output may sit
+    half a unit from the common fp32 value; 1 ulp <= |b| * 2^-7), and the
+    mean-relative bar as in assert_parity."""
+    a = mo.bf16_bits_to_f32(a_bf16_bits).astype(np.float64)
+    b = mo.bf16_bits_to_f32(b_bf16_bits).astype(np.float64)
+    err = np.abs(a - b)
+    bound = max_abs + np.abs(b) * 2.0 ** -7
+    worst = int(np.argmax(err - bound))
+    assert (err <= bound).all(), f"|a-b| {err.flat[worst]:.3e} > {bound.flat[worst]:.3e} at |b| {abs(b.flat[worst]):.3e}"
+    denom = np.abs(b).mean() + 1e-30
+    assert err.mean() / denom <= mean_rel, f"mean-rel {err.mean() / denom:.3e} > {mean_rel}"
