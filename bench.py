@@ -58,6 +58,11 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=960)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--prefill", default="mixtral,qwen2",
+                    help="prefill workloads to report beside the decode line: mixtral (config 3), qwen2 (config 4)")
+    ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--skip-decode", action="store_true",
+                    help="report only the prefill workloads (profiling runs of the grouped GEMM)")
     return ap.parse_args()
 
 
@@ -469,6 +474,13 @@ def main():
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=dev).manual_seed(args.seed + 1000 * rank)
+    if args.skip_decode:
+        pre = prefill_block(args, dev, rank)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "n_gpus": world, "data": "synthetic", "prefill": pre}), flush=True)
+        if torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+        return
     uniq = [make_unique_layer(gen, dev) for _ in range(min(UNIQUE_LAYERS, args.layers))]
     lws = [uniq[i] if i < len(uniq) else clone_layer(uniq[i % len(uniq)]) for i in range(args.layers)]
     max_b = max([args.batch] + [int(b) for b in args.sweep.split(",") if b])
@@ -538,6 +550,10 @@ def main():
     if sweep:
         line["sweep"] = sweep
 
+    pre = prefill_block(args, dev, rank)
+    if pre:
+        line["prefill"] = pre
+
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, n, busy = cpu_reference_rate(lws, x, logits, args.cpu_seconds, 10 ** 6)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
@@ -549,6 +565,153 @@ def main():
         print(json.dumps(line), flush=True)
     if torch.distributed.is_initialized():
         torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# prefill workloads (tensor-core grouped GEMM path)
+# ---------------------------------------------------------------------------
+
+PREFILL = {
+    # config 3: Mixtral-8x7B-shaped layer, 2048-token prefill, W8 per-channel,
+    # top-2 softmax over the top-k logits
+    "mixtral": dict(experts=8, hidden=4096, inter=14336, top_k=2, bits=8, group=0, softmax=False, renorm=True,
+                    tokens=2048, shared=0, zipf=None),
+    # config 4: Qwen2-MoE-A2.7B-shaped layer, 256 tokens, W4 g128, top-4 without
+    # renormalisation, shared expert 5632 with a sigmoid gate, Zipf(1.2) routing
+    "qwen2": dict(experts=60, hidden=2048, inter=1408, top_k=4, bits=4, group=128, softmax=True, renorm=False,
+                  tokens=256, shared=5632, zipf=1.2),
+}
+
+
+def quantized_stack(gen, device, E, n, k, bits, group):
+    """[E, n, k*bits/8] codes + padded bf16 scales of N(0, 0.02) weights."""
+    import torch
+
+    from nano_ktrans_b200.weights import quantize_symmetric, scale_stride
+
+    g = group if group > 0 else k
+    q = torch.empty(E, n, k * bits // 8, dtype=torch.uint8, device=device)
+    s = torch.zeros(E, n, scale_stride(k // g), dtype=torch.bfloat16, device=device)
+    for e in range(E):
+        qw = quantize_symmetric(torch.randn(n, k, generator=gen, device=device) * 0.02, group_size=group, bits=bits)
+        q[e] = qw.qweight.view(torch.uint8).view(n, -1)
+        s[e, :, :k // g] = qw.scales.view(n, -1).to(torch.bfloat16)
+        del qw
+    return q, s
+
+
+def zipf_router_bias(E: int, alpha: float, gen, device):
+    """b_e = log(z_e), z proportional to rank^-alpha over a seeded expert permutation."""
+    import torch
+
+    perm = torch.randperm(E, generator=gen, device=device)
+    ranks = torch.empty(E, device=device)
+    ranks[perm] = torch.arange(1, E + 1, device=device, dtype=torch.float32)
+    z = ranks ** (-alpha)
+    return torch.log(z / z.sum())
+
+
+def bf16_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_prefill(name: str, gen, device, steps: int, warmup: int):
+    """Device time of MoeLayer.forward (route + permute + pack + grouped GEMMs +
+    combine, shared expert included) on one prefill batch, CUDA events on the
+    launching stream; the expert weights (> L2) are re-read every step."""
+    import torch
+
+    from nano_ktrans_b200 import _lib
+    from nano_ktrans_b200.moe_layer import MoeLayer
+    from nano_ktrans_b200.weights import LayerWeights
+
+    c = PREFILL[name]
+    E, H, I, k, T, bits, grp = c["experts"], c["hidden"], c["inter"], c["top_k"], c["tokens"], c["bits"], c["group"]
+    gq, gs = quantized_stack(gen, device, E, I, H, bits, grp)
+    uq, us = quantized_stack(gen, device, E, I, H, bits, grp)
+    dq, ds = quantized_stack(gen, device, E, H, I, bits, grp)
+    shared = None
+    if c["shared"]:
+        S = c["shared"]
+        sg = quantized_stack(gen, device, 1, S, H, bits, grp)
+        su = quantized_stack(gen, device, 1, S, H, bits, grp)
+        sd = quantized_stack(gen, device, 1, H, S, bits, grp)
+        vec = (torch.randn(H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+        shared = {"gate_q": sg[0], "gate_s": sg[1], "up_q": su[0], "up_s": su[1], "down_q": sd[0], "down_s": sd[1],
+                  "gate_vec": vec}
+    lw = LayerWeights(bits=bits, group_size=grp, gate_q=gq, gate_s=gs, up_q=uq, up_s=us, down_q=dq, down_s=ds,
+                      shared=shared)
+    layer = MoeLayer(lw, top_k=k, router_use_softmax=c["softmax"], normalize_topk_prob=c["renorm"], max_tokens=T)
+    x = torch.randn(T, H, generator=gen, device=device).to(torch.bfloat16)
+    wr = (torch.randn(E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    logits = x @ wr.T
+    if c["zipf"]:
+        logits = (logits.float() + zipf_router_bias(E, c["zipf"], gen, device)).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    for _ in range(max(warmup, 3)):
+        layer.forward(x, logits, out=out)
+    torch.cuda.synchronize()
+    launches = layer.last_launch_count()
+    kern = {}
+    for cls, nm in ((_lib.K_GATEUP, "gateup"), (_lib.K_DOWN, "down")):
+        layer.profile_begin(cls, steps)
+        for _ in range(steps):
+            layer.forward(x, logits, out=out)
+        ms_k, n_k = layer.profile_end()
+        kern[nm] = ms_k / max(n_k, 1)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(steps):
+        layer.forward(x, logits, out=out)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    ids, _ = layer.route(logits)
+    per_expert = torch.bincount(ids.reshape(-1), minlength=E)
+    flops_routed = 2.0 * T * k * 3 * H * I
+    flops_gateup = 2.0 * T * k * 2 * H * I
+    peak, peak_kind = bf16_peak()
+    gu_tf = flops_gateup / (kern["gateup"] / 1e3) / 1e12
+    res = {
+        "config": f"{name}: E={E} H={H} I={I} top{k} W{bits} group={grp or 'per-channel'} tokens={T}"
+                  + (f" shared={c['shared']} zipf={c['zipf']}" if c["shared"] else ""),
+        "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "launches_per_step": launches,
+        "routed_tflops": flops_routed / (ms / 1e3) / 1e12,
+        "tokens_per_expert": {"max": int(per_expert.max()), "min": int(per_expert.min()),
+                              "mean": float(per_expert.float().mean())},
+        "roofline": {"bound": "tensor", "kernel": f"grouped_gemm_kernel<{bits},gate/up>", "achieved": gu_tf,
+                     "peak": peak, "unit": "TFLOP/s", "frac": gu_tf / peak, "peak_source": peak_kind,
+                     "algorithmic_flops_per_launch": flops_gateup, "avg_launch_ms": kern["gateup"]},
+        "down_kernel_tflops": 2.0 * T * k * H * I / (kern["down"] / 1e3) / 1e12,
+        "down_avg_launch_ms": kern["down"],
+    }
+    del layer, lw, gq, gs, uq, us, dq, ds
+    torch.cuda.empty_cache()
+    return res
+
+
+def prefill_block(args, dev, rank):
+    """Prefill workloads, one replica per rank; ms is the max over ranks."""
+    import torch
+
+    out = {}
+    for name in [n for n in args.prefill.split(",") if n]:
+        gen = torch.Generator(device=dev).manual_seed(args.seed + 17 + 1000 * rank)
+        r = run_prefill(name, gen, dev, args.prefill_steps, args.warmup)
+        ms = max_over_ranks(r["ms_per_step"])
+        world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
+        r["ms_per_step"] = ms
+        r["tokens_per_s"] = PREFILL[name]["tokens"] * world / (ms / 1e3)
+        r["replicas"] = world
+        out[name] = r
+    return out
 
 
 def read_traffic(kernel: str, batch: int):

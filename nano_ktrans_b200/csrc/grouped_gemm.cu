@@ -43,8 +43,24 @@ namespace gg {
 constexpr int BM = kGemmBM;  // weight rows per tile
 constexpr int BN = kGemmBN;  // tokens per tile
 constexpr int BK = kGemmBK;  // K per stage (one 128-byte fp16 row)
-constexpr int kThreads = 192;
 constexpr uint32_t kSpin = 1u << 22;  // bounded waits: the kernel records kStatusTimeout and unwinds
+
+#ifdef MOE_GEMM_TRACE
+// Instrumented builds only: per-CTA %globaltimer stamps of the last launch.
+constexpr int kTraceCtas = 1 << 15;
+__device__ unsigned long long g_gemm_trace[2][kTraceCtas][8];  // [down, gate/up][cta][stamp]
+template <bool GATEUP>
+MOE_DEV void stamp(int i) {
+  if (blockIdx.x < kTraceCtas) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_gemm_trace[GATEUP ? 1 : 0][blockIdx.x][i] = t;
+  }
+}
+#define GG_STAMP(i) stamp<GATEUP>(i)
+#else
+#define GG_STAMP(i) ((void)0)
+#endif
 
 MOE_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -180,58 +196,89 @@ struct GemmArgs {
   int* status;
 };
 
+// Shared-memory plan.  Two rings:
+//   load ring  (kLS stages): activation tile [BN][64] fp16 + code tile(s) [BM][64*BITS/8], filled by TMA;
+//   operand ring (2 stages): dequantized weight tile(s) [BM][64] fp16, written by the dequant warps.
+// A load stage is released when the MMAs that read it complete, which is after
+// the dequant warps consumed its codes (the MMAs wait for their operands).
 template <int BITS, bool GATEUP>
-struct Smem {
+struct Plan {
   static constexpr int kCodeRow = BK * BITS / 8;  // code bytes per row per stage
-  static constexpr int kX = BN * 128;             // activation tile
-  static constexpr int kA = BM * 128;             // dequantized weight tile
-  static constexpr int kC = BM * kCodeRow;        // code tile
   static constexpr int kNP = GATEUP ? 2 : 1;
-  static constexpr int kStage = kX + kNP * (kA + kC);
-  static constexpr int kStages = GATEUP ? 3 : 4;
-  static constexpr int kBarOff = kStages * kStage;
-  static constexpr int kBytes = kBarOff + 256 + 1024;  // barriers + TMEM slot + alignment slack
+  static constexpr int kX = BN * 128;             // activation tile
+  static constexpr int kC = BM * kCodeRow;        // code tile, per projection
+  static constexpr int kA = BM * 128;             // dequantized tile, per projection
+  static constexpr int kLoad = kX + kNP * kC;
+  static constexpr int kOper = kNP * kA;
+  static constexpr int kOS = 2;
+  static constexpr int kBudget = 232448 - 2048;   // opt-in limit minus barriers and alignment slack
+  static constexpr int kLSraw = (kBudget - kOS * kOper) / kLoad;
+  static constexpr int kLS = kLSraw > 8 ? 8 : kLSraw;
+  static constexpr int kOperOff = kLS * kLoad;    // multiple of 1024
+  static constexpr int kBarOff = kOperOff + kOS * kOper;
+  static constexpr int kNumBars = 2 * kLS + 2 * kOS + 1;
+  static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;
+  static_assert(kLS >= 3, "load ring too shallow");
+  static_assert(kLoad % 1024 == 0 && kOper % 1024 == 0, "tiles must stay 1024-byte aligned");
+  static_assert(kBytes <= 232448, "shared-memory plan exceeds the opt-in limit");
 };
 
+constexpr int kDqWarps = 8;                         // dequant + epilogue warps (2 per TMEM lane quarter)
+constexpr int kThreadsV2 = 64 + 32 * kDqWarps;      // + producer warp + MMA warp
+
 template <int BITS, bool GATEUP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsV2, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w0,
                         const __grid_constant__ CUtensorMap tm_w1, GemmArgs a) {
-  using L = Smem<BITS, GATEUP>;
+  using L = Plan<BITS, GATEUP>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // ---- tile -> (expert, token tile, feature block) ----
+  // ---- CTA -> (expert, feature block, token tile) ----
+  // Expert-major, then feature block, token tiles fastest: the CTAs that
+  // share one weight tile run side by side, so it leaves HBM once and the
+  // other token tiles read it from L2.
   const int nfb = a.N / BM;
-  const int fb = blockIdx.x % nfb, tt = blockIdx.x / nfb;
   const int n_act = *a.n_active;
-  if (tt >= a.tile_off[n_act]) return;  // CTA-uniform, before any barrier
-  int lo = 0, hi = n_act;               // tile_off[lo] <= tt < tile_off[hi]
+  const int g = blockIdx.x;
+  if (g >= a.tile_off[n_act] * nfb) return;  // CTA-uniform, before any barrier
+  int lo = 0, hi = n_act;                    // tile_off[lo]*nfb <= g < tile_off[hi]*nfb
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (a.tile_off[mid] <= tt) lo = mid;
+    if (a.tile_off[mid] * nfb <= g) lo = mid;
     else hi = mid;
   }
+  const int tiles = a.tile_off[lo + 1] - a.tile_off[lo];
+  const int local = g - a.tile_off[lo] * nfb;
+  const int fb = local / tiles, tt = local - fb * tiles;
   const int e = a.active[lo];
-  const int s_begin = a.offsets[e] + (tt - a.tile_off[lo]) * BN;
+  const int s_begin = a.offsets[e] + tt * BN;
   const int ntok = min(BN, a.offsets[e + 1] - s_begin);
   const int wrow = e * a.N + fb * BM;  // first weight row (codes tensor row)
   const int nk = a.K / BK;
+  if (tid == 0) GG_STAMP(0);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  // full[s] = bars[s], afull[s] = bars[kStages + s], empty[s] = bars[2*kStages + s], acc = bars[3*kStages]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBarOff + 8 * (3 * L::kStages + 1));
+  uint64_t* load_full = bars;                   // [kLS]  TMA bytes landed
+  uint64_t* load_empty = bars + L::kLS;         // [kLS]  MMAs reading the stage completed
+  uint64_t* oper_full = bars + 2 * L::kLS;      // [kOS]  256 dequant threads wrote the operand
+  uint64_t* oper_empty = oper_full + L::kOS;    // [kOS]  MMAs reading the operand completed
+  uint64_t* acc_full = oper_empty + L::kOS;     // [1]    last MMA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   __shared__ int abort_flag_s;
   volatile int* abort_flag = &abort_flag_s;  // set by whichever role times out first
 
   if (tid == 0) {
-    for (int s = 0; s < L::kStages; ++s) {
-      mbar_init(smem_u32(&bars[s]), 1);
-      mbar_init(smem_u32(&bars[L::kStages + s]), 128);
-      mbar_init(smem_u32(&bars[2 * L::kStages + s]), 1);
+    for (int s = 0; s < L::kLS; ++s) {
+      mbar_init(smem_u32(&load_full[s]), 1);
+      mbar_init(smem_u32(&load_empty[s]), 1);
     }
-    mbar_init(smem_u32(&bars[3 * L::kStages]), 1);
+    for (int s = 0; s < L::kOS; ++s) {
+      mbar_init(smem_u32(&oper_full[s]), 32 * kDqWarps);
+      mbar_init(smem_u32(&oper_empty[s]), 1);
+    }
+    mbar_init(smem_u32(acc_full), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_flag = 0;
   }
@@ -244,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  if (tid == 0) GG_STAMP(1);
 
   auto give_up = [&]() {
     if (!*abort_flag) {
@@ -251,71 +299,75 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicOr(a.status, kStatusTimeout);
     }
   };
-  auto stage_ptr = [&](int s) { return smem + s * L::kStage; };
-  // stage layout: X | A0 | C0 | A1 | C1
-  auto x_tile = [&](int s) { return stage_ptr(s); };
-  auto a_tile = [&](int s, int p) { return stage_ptr(s) + L::kX + p * (L::kA + L::kC); };
-  auto c_tile = [&](int s, int p) { return stage_ptr(s) + L::kX + p * (L::kA + L::kC) + L::kA; };
+  // load stage: X | C0 | C1 ; operand stage: A0 | A1
+  auto x_tile = [&](int s) { return smem + s * L::kLoad; };
+  auto c_tile = [&](int s, int p) { return smem + s * L::kLoad + L::kX + p * L::kC; };
+  auto a_tile = [&](int s, int p) { return smem + L::kOperOff + s * L::kOper + p * L::kA; };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int issued = 0;
       for (int c = 0; c < nk && !*abort_flag; ++c) {
-        const int s = c % L::kStages;
-        if (c >= L::kStages &&
-            !mbar_wait(smem_u32(&bars[2 * L::kStages + s]), static_cast<uint32_t>(((c / L::kStages) - 1) & 1))) {
+        const int s = c % L::kLS;
+        if (c >= L::kLS && !mbar_wait(smem_u32(&load_empty[s]), static_cast<uint32_t>(((c / L::kLS) - 1) & 1))) {
           give_up();
           break;
         }
-        const uint32_t full = smem_u32(&bars[s]);
-        mbar_expect_tx(full, static_cast<uint32_t>(L::kX + L::kNP * L::kC));
+        const uint32_t full = smem_u32(&load_full[s]);
+        mbar_expect_tx(full, static_cast<uint32_t>(L::kLoad));
         tma_load_2d(smem_u32(x_tile(s)), &tm_x, c * BK, s_begin, full);
         tma_load_2d(smem_u32(c_tile(s, 0)), &tm_w0, c * L::kCodeRow, wrow, full);
         if constexpr (GATEUP) tma_load_2d(smem_u32(c_tile(s, 1)), &tm_w1, c * L::kCodeRow, wrow, full);
         issued = c + 1;
       }
+      GG_STAMP(4);
       if (*abort_flag) {
         // no copy may still be landing in shared memory when the CTA exits
-        for (int c = max(0, issued - L::kStages); c < issued; ++c)
-          mbar_wait(smem_u32(&bars[c % L::kStages]), static_cast<uint32_t>((c / L::kStages) & 1));
+        for (int c = max(0, issued - L::kLS); c < issued; ++c)
+          mbar_wait(smem_u32(&load_full[c % L::kLS]), static_cast<uint32_t>((c / L::kLS) & 1));
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       for (int c = 0; c < nk && !*abort_flag; ++c) {
-        const int s = c % L::kStages;
-        const uint32_t par = static_cast<uint32_t>((c / L::kStages) & 1);
-        if (!mbar_wait(smem_u32(&bars[L::kStages + s]), par) || !mbar_wait(smem_u32(&bars[s]), par)) {
+        const int s = c % L::kLS, o = c % L::kOS;
+        if (!mbar_wait(smem_u32(&oper_full[o]), static_cast<uint32_t>((c / L::kOS) & 1)) ||
+            !mbar_wait(smem_u32(&load_full[s]), static_cast<uint32_t>((c / L::kLS) & 1))) {
           give_up();
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (c == 0) GG_STAMP(2);
         const uint64_t db = sw128_desc(smem_u32(x_tile(s)));
-        const uint64_t da0 = sw128_desc(smem_u32(a_tile(s, 0)));
-        const uint64_t da1 = GATEUP ? sw128_desc(smem_u32(a_tile(s, 1))) : 0;
+        const uint64_t da0 = sw128_desc(smem_u32(a_tile(o, 0)));
+        const uint64_t da1 = GATEUP ? sw128_desc(smem_u32(a_tile(o, 1))) : 0;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
           umma_f16(tmem, da0 + 2 * kk, db + 2 * kk, acc);  // +32 bytes per K step of 16
           if constexpr (GATEUP) umma_f16(tmem + BN, da1 + 2 * kk, db + 2 * kk, acc);
         }
-        umma_commit(smem_u32(&bars[2 * L::kStages + s]));
+        umma_commit(smem_u32(&load_empty[s]));
+        umma_commit(smem_u32(&oper_empty[o]));
       }
-      umma_commit(smem_u32(&bars[3 * L::kStages]));
+      GG_STAMP(3);
+      umma_commit(smem_u32(acc_full));
       // every MMA has finished (normal or aborted) before TMEM is released
-      if (!mbar_wait(smem_u32(&bars[3 * L::kStages]), 0u)) give_up();
+      if (!mbar_wait(smem_u32(acc_full), 0u)) give_up();
     }
   } else {
-    // ---------------- dequant (warps 2-5), then epilogue ----------------
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int r = quarter * 32 + lane;
+    // ---------------- dequant (warps 2-9), then epilogue ----------------
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;        // which half of the K chunk / of the token columns
+    const int r = quarter * 32 + lane;       // weight row within the tile
     const size_t srow = static_cast<size_t>(wrow + r) * a.sstride;
     for (int c = 0; c < nk; ++c) {
-      const int s = c % L::kStages;
+      const int s = c % L::kLS, o = c % L::kOS;
       if (*abort_flag) break;
-      if (!mbar_wait(smem_u32(&bars[s]), static_cast<uint32_t>((c / L::kStages) & 1))) {
+      if (!mbar_wait(smem_u32(&load_full[s]), static_cast<uint32_t>((c / L::kLS) & 1)) ||
+          (c >= L::kOS && !mbar_wait(smem_u32(&oper_empty[o]), static_cast<uint32_t>(((c / L::kOS) - 1) & 1)))) {
         give_up();
         break;
       }
@@ -326,30 +378,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint16_t* sp = p == 0 ? a.s0 : a.s1;
           sc = __float2half2_rn(bf16_to_f32(__ldg(sp + srow + (c * BK) / a.group)));
         }
-        const uint4* codes = reinterpret_cast<const uint4*>(c_tile(s, p) + r * L::kCodeRow);
-        unsigned char* arow = a_tile(s, p) + r * 128;
+        // this thread's half of the row: 16 code bytes (W4) or 32 (W8) -> output chunks 4*half .. 4*half+3
+        const uint4* codes = reinterpret_cast<const uint4*>(c_tile(s, p) + r * L::kCodeRow + half * (L::kCodeRow / 2));
+        unsigned char* arow = a_tile(o, p) + r * 128;
+        constexpr int kVec = L::kCodeRow / 32;  // uint4 code vectors per half row
+        constexpr int kOut = 4 / kVec;           // output chunks per code vector
 #pragma unroll
-        for (int j = 0; j < L::kCodeRow / 16; ++j) {
-          uint4 o[BITS == 4 ? 4 : 2];
-          dequant16<BITS>(codes[j], sc, o);
+        for (int j = 0; j < kVec; ++j) {
+          uint4 ov[kOut];
+          dequant16<BITS>(codes[j], sc, ov);
 #pragma unroll
-          for (int q = 0; q < (BITS == 4 ? 4 : 2); ++q) {
-            const int chunk = j * (BITS == 4 ? 4 : 2) + q;  // 16-byte chunk of the 128-byte row
-            *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = o[q];
+          for (int q = 0; q < kOut; ++q) {
+            const int chunk = 4 * half + j * kOut + q;  // 16-byte chunk of the 128-byte row
+            *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = ov[q];
           }
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-      mbar_arrive(smem_u32(&bars[L::kStages + s]));
+      mbar_arrive(smem_u32(&oper_full[o]));
     }
-    // epilogue
+    // epilogue: this warp's 32 rows x 64 token columns
     bool ok = !*abort_flag;
-    if (ok && !mbar_wait(smem_u32(&bars[3 * L::kStages]), 0u)) {
+    if (ok && !mbar_wait(smem_u32(acc_full), 0u)) {
       give_up();
       ok = false;
     }
     if (ok && !*abort_flag) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (warp == 2 && lane == 0) GG_STAMP(5);
       const uint32_t tl = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row = fb * BM + r;  // feature row within the expert
       float s0w = 1.0f, s1w = 1.0f;
@@ -358,19 +414,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (GATEUP) s1w = bf16_to_f32(__ldg(a.s1 + srow));
       }
       const int col = GATEUP ? (row & ~7) + kpos<BITS>(row & 7) : row;
-      for (int j = 0; j < BN / 16; ++j) {
+      const int n0 = half * (BN / 2);
+      for (int j = 0; j < BN / 32; ++j) {
+        const int nb = n0 + j * 16;
+        if (nb >= ntok) break;  // warp-uniform
         float d0[16], d1[16];
-        tmem_ld16(tl + j * 16, d0);
-        if constexpr (GATEUP) tmem_ld16(tl + BN + j * 16, d1);
+        tmem_ld16(tl + nb, d0);
+        if constexpr (GATEUP) tmem_ld16(tl + BN + nb, d1);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int n = j * 16 + i;
+          const int n = nb + i;
           if (n < ntok) {
-            const size_t o = static_cast<size_t>(s_begin + n) * a.N + col;
+            const size_t oidx = static_cast<size_t>(s_begin + n) * a.N + col;
             if constexpr (GATEUP) {
-              a.hout[o] = __float2half_rn(silu_f32(d0[i] * s0w) * (d1[i] * s1w));
+              a.hout[oidx] = __float2half_rn(silu_f32(d0[i] * s0w) * (d1[i] * s1w));
             } else {
-              a.yout[o] = d0[i] * s0w;
+              a.yout[oidx] = d0[i] * s0w;
             }
           }
         }
@@ -383,6 +442,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::kNP * BN));
   }
+#ifdef MOE_GEMM_TRACE
+  if (tid == 0) {
+    GG_STAMP(6);
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    if (blockIdx.x < kTraceCtas)
+      g_gemm_trace[GATEUP ? 1 : 0][blockIdx.x][7] = smid | (static_cast<unsigned long long>(ntok) << 32);
+  }
+#endif
 }
 
 // Token-tile prefix over the active experts: tile_off[a] = sum_{a' < a} ceil(count / BN).
@@ -487,7 +555,7 @@ void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, in
 
 template <int BITS, bool GATEUP>
 static int launch_gemm_t(const GemmLaunch& g, cudaStream_t st) {
-  using L = gg::Smem<BITS, GATEUP>;
+  using L = gg::Plan<BITS, GATEUP>;
   auto kern = gg::grouped_gemm_kernel<BITS, GATEUP>;
   static int configured = 0;
   int dev = 0;
@@ -515,7 +583,7 @@ static int launch_gemm_t(const GemmLaunch& g, cudaStream_t st) {
   const CUtensorMap* tx = reinterpret_cast<const CUtensorMap*>(g.tmap_x);
   const CUtensorMap* t0 = reinterpret_cast<const CUtensorMap*>(g.tmap_w0);
   const CUtensorMap* t1 = reinterpret_cast<const CUtensorMap*>(GATEUP ? g.tmap_w1 : g.tmap_w0);
-  kern<<<grid, gg::kThreads, L::kBytes, st>>>(*tx, *t0, *t1, a);
+  kern<<<grid, gg::kThreadsV2, L::kBytes, st>>>(*tx, *t0, *t1, a);
   return 1;
 }
 
@@ -525,3 +593,9 @@ int launch_grouped_gemm(int bits, bool gateup, const GemmLaunch& g, cudaStream_t
 }
 
 }  // namespace moe
+
+#ifdef MOE_GEMM_TRACE
+extern "C" int moe_gemm_trace_copy(void* host, size_t bytes) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, moe::gg::g_gemm_trace, bytes));
+}
+#endif
