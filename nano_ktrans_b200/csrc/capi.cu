@@ -51,6 +51,14 @@ struct Handle {
   alignas(64) unsigned char tm_gate[128];  // uint8 [E*I][H*bits/8]
   alignas(64) unsigned char tm_up[128];
   alignas(64) unsigned char tm_down[128];  // uint8 [E*H][I*bits/8]
+  // shared expert on the GEMM path
+  bool shared_gemm_maps = false;
+  int32_t* sh_tables = nullptr;             // int32[6]: one-expert tables over T tokens
+  alignas(64) unsigned char tm_sx[128];     // fp16 [max_tokens][H] over sh_y
+  alignas(64) unsigned char tm_sh[128];     // fp16 [max_tokens][S] over sh_h
+  alignas(64) unsigned char tm_sgate[128];  // uint8 [S][H*bits/8]
+  alignas(64) unsigned char tm_sup[128];
+  alignas(64) unsigned char tm_sdown[128];  // uint8 [H][S*bits/8]
   std::string err;
   int last_launches = 0;
   // profiling: events bracketing one kernel class
@@ -153,6 +161,23 @@ bool encode_gemm_maps(Handle* h) {
                                static_cast<uint64_t>(E) * I, code_box, moe::kGemmBM, false);
   ok = ok && moe::make_tmap_2d(h->tm_down, h->w.down_q_dev, false, static_cast<uint64_t>(I) * bits / 8,
                                static_cast<uint64_t>(E) * H, code_box, moe::kGemmBM, false);
+  h->shared_gemm_maps = false;
+  const int S = d.shared_inter;
+  if (ok && S > 0) {
+    const QuantProj sg = make_proj(h, h->w.shared_gate_q_dev, h->w.shared_gate_s_dev, S, H);
+    const QuantProj sd = make_proj(h, h->w.shared_down_q_dev, h->w.shared_down_s_dev, H, S);
+    const uint64_t T = static_cast<uint64_t>(d.max_tokens);
+    bool sok = moe::gemm_shape_ok(bits, sg) && moe::gemm_shape_ok(bits, sd);
+    sok = sok && moe::make_tmap_2d(h->tm_sx, h->sh_y, true, H, T, moe::kGemmBK, moe::kGemmBN, true);
+    sok = sok && moe::make_tmap_2d(h->tm_sh, h->sh_h, true, S, T, moe::kGemmBK, moe::kGemmBN, true);
+    sok = sok && moe::make_tmap_2d(h->tm_sgate, h->w.shared_gate_q_dev, false, static_cast<uint64_t>(H) * bits / 8,
+                                   S, code_box, moe::kGemmBM, false);
+    sok = sok && moe::make_tmap_2d(h->tm_sup, h->w.shared_up_q_dev, false, static_cast<uint64_t>(H) * bits / 8, S,
+                                   code_box, moe::kGemmBM, false);
+    sok = sok && moe::make_tmap_2d(h->tm_sdown, h->w.shared_down_q_dev, false, static_cast<uint64_t>(S) * bits / 8,
+                                   H, code_box, moe::kGemmBM, false);
+    h->shared_gemm_maps = sok;
+  }
   return ok;
 }
 
@@ -196,7 +221,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
                o_nact = take(4), o_sorted = take(4 * P), o_pos = take(4 * P), o_h = take(4 * P * I),
                o_y = take(4 * P * H), o_shh = take(S ? 4 * T * S : 0), o_shy = take(S ? 4 * T * H : 0),
                o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P), o_bar = take(8),
-               o_tiles = take(4 * (E + 1));
+               o_tiles = take(4 * (E + 1)), o_shtab = take(4 * 8);
   h->ws_bytes = off;
   cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
   if (e != cudaSuccess) {
@@ -223,6 +248,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   h->w_tmp = reinterpret_cast<uint16_t*>(b + o_w);
   h->grid_bar = reinterpret_cast<unsigned long long*>(b + o_bar);
   h->tile_off = reinterpret_cast<int32_t*>(b + o_tiles);
+  h->sh_tables = reinterpret_cast<int32_t*>(b + o_shtab);
   e = cudaMemset(h->ws, 0, h->ws_bytes);
   if (e != cudaSuccess) {
     fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
@@ -338,10 +364,16 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
   const QuantProj down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
   if (h->gemm_mode == 2 && !h->gemm_maps)
     return fail(h, MOE_EINVAL, "GEMM path forced but this layer's shape is outside its rules");
-  if (use_gemm(h, T)) {
-    moe::launch_tile_table(h->rt, h->tile_off, st);
+  const bool shared_gemm = add_shared && d.shared_inter > 0 && h->shared_gemm_maps && h->gemm_mode != 0 &&
+                           (h->gemm_mode == 2 || T >= 16);
+  const bool routed_gemm = use_gemm(h, T);
+  if (routed_gemm || shared_gemm) {
+    moe::launch_tile_table(h->rt, h->tile_off, shared_gemm ? h->sh_tables : nullptr, T, st);
+    ++launches;
+  }
+  if (routed_gemm) {
     moe::launch_pack_x(d.bits, x, h->rt, E, k, 0, H, T * k, h->ybuf, h->num_sms, st);
-    launches += 2;
+    ++launches;
     moe::GemmLaunch g{};
     g.rt = h->rt;
     g.tile_off = h->tile_off;
@@ -387,8 +419,39 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     const QuantProj sdp = make_proj(h, h->w.shared_down_q_dev, h->w.shared_down_s_dev, H, S);
     moe::launch_shared_gate(x, static_cast<const uint16_t*>(h->w.shared_gate_vec_dev), T, H, h->sh_g, st);
     ++launches;
-    launches += moe::launch_gateup(d.bits, x, h->rt, 1, 1, T, T, sgp, sup, h->sh_h, h->num_sms, st);
-    launches += moe::launch_down(d.bits, h->sh_h, h->rt, 1, T, T, sdp, h->sh_y, h->num_sms, st);
+    if (shared_gemm) {
+      // one expert over tokens 0..T-1; x (fp16) staged in sh_y, which the down GEMM overwrites afterwards
+      moe::launch_pack_x(d.bits, x, h->rt, E, k, T, H, T, h->sh_y, h->num_sms, st);
+      moe::GemmLaunch g{};
+      g.rt.offsets = h->sh_tables;
+      g.rt.active = h->sh_tables + 2;
+      g.rt.n_active = h->sh_tables + 3;
+      g.tile_off = h->sh_tables + 4;
+      g.status = h->rt.status;
+      g.max_pairs = T;
+      g.max_active = 1;
+      g.p0 = sgp;
+      g.p1 = sup;
+      g.tmap_x = h->tm_sx;
+      g.tmap_w0 = h->tm_sgate;
+      g.tmap_w1 = h->tm_sup;
+      g.hout = h->sh_h;
+      int rc = moe::launch_grouped_gemm(d.bits, true, g, st);
+      if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (shared gate/up): shared-memory opt-in refused");
+      g.p0 = sdp;
+      g.p1 = sdp;
+      g.tmap_x = h->tm_sh;
+      g.tmap_w0 = h->tm_sdown;
+      g.tmap_w1 = h->tm_sdown;
+      g.hout = nullptr;
+      g.yout = h->sh_y;
+      rc = moe::launch_grouped_gemm(d.bits, false, g, st);
+      if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (shared down): shared-memory opt-in refused");
+      launches += 3;
+    } else {
+      launches += moe::launch_gateup(d.bits, x, h->rt, 1, 1, T, T, sgp, sup, h->sh_h, h->num_sms, st);
+      launches += moe::launch_down(d.bits, h->sh_h, h->rt, 1, T, T, sdp, h->sh_y, h->num_sms, st);
+    }
     sg = h->sh_g;
     sy = h->sh_y;
   }

@@ -454,8 +454,12 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
 }
 
 // Token-tile prefix over the active experts: tile_off[a] = sum_{a' < a} ceil(count / BN).
+// With shared != nullptr also writes the one-expert tables of the shared
+// expert over tokens 0..T-1: offsets {0, T}, active {0}, n_active 1,
+// tile_off {0, ceil(T / BN)}.
 __global__ void tile_table_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                                  const int32_t* __restrict__ n_active, int32_t* __restrict__ tile_off) {
+                                  const int32_t* __restrict__ n_active, int32_t* __restrict__ tile_off,
+                                  int32_t* __restrict__ shared, int T) {
   if (threadIdx.x != 0) return;
   const int n = *n_active;
   int acc = 0;
@@ -465,6 +469,14 @@ __global__ void tile_table_kernel(const int32_t* __restrict__ offsets, const int
     acc += (offsets[e + 1] - offsets[e] + BN - 1) / BN;
   }
   tile_off[n] = acc;
+  if (shared != nullptr) {
+    shared[0] = 0;  // offsets
+    shared[1] = T;
+    shared[2] = 0;  // active
+    shared[3] = 1;  // n_active
+    shared[4] = 0;  // tile_off
+    shared[5] = (T + BN - 1) / BN;
+  }
 }
 
 // X16[s][k'] = fp16(x[token(s)][k]) with k permuted within each group of 8 (kpos).
@@ -537,8 +549,8 @@ bool gemm_shape_ok(int bits, const QuantProj& p) {
   return true;
 }
 
-void launch_tile_table(const RouteTables& rt, int32_t* tile_off, cudaStream_t st) {
-  gg::tile_table_kernel<<<1, 32, 0, st>>>(rt.offsets, rt.active, rt.n_active, tile_off);
+void launch_tile_table(const RouteTables& rt, int32_t* tile_off, int32_t* shared_tables, int T, cudaStream_t st) {
+  gg::tile_table_kernel<<<1, 32, 0, st>>>(rt.offsets, rt.active, rt.n_active, tile_off, shared_tables, T);
 }
 
 void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, int top_k, int identity_tokens, int H,

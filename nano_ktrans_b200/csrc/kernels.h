@@ -105,7 +105,10 @@ struct GemmLaunch {
   int max_pairs;            // upper bound of the pair count of this call
   int max_active;           // upper bound of the active expert count of this call
 };
-void launch_tile_table(const RouteTables& rt, int32_t* tile_off, cudaStream_t st);
+// tile_off over the active experts; with shared_tables != nullptr also the
+// int32[6] one-expert tables of the shared expert over T tokens: offsets[2],
+// active[1], n_active[1], tile_off[2].
+void launch_tile_table(const RouteTables& rt, int32_t* tile_off, int32_t* shared_tables, int T, cudaStream_t st);
 // x16[s] = fp16(x[token of sorted pair s]) with K permuted to the dequant order.
 void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, int top_k, int identity_tokens, int H,
                    int max_pairs, void* x16, int num_sms, cudaStream_t st);
