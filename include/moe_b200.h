@@ -134,6 +134,41 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
                 int32_t num_tokens, uint16_t* out_dev, int64_t* topk_ids_dev,
                 uint16_t* topk_weights_dev, void* stream);
 
+/* ---- Expert parallelism (no counterpart in the reference, whose offload
+ * backends are single-device) ----
+ * The routed experts are split over `world` ranks; expert e lives on rank
+ * slot_of_expert[e] / experts_per_rank as local expert
+ * slot_of_expert[e] % experts_per_rank (slot_of_expert is a permutation of
+ * 0..num_experts-1, world * experts_per_rank == num_experts).  The three
+ * calls below are the device steps; the exchanges between them are two
+ * all-to-alls the caller runs (NCCL all_to_all_single):
+ *   1. moe_ep_dispatch on the token's rank (handle with the layer's
+ *      num_experts / top_k): sorts the T*k (token, slot) pairs by slot
+ *      (= by destination rank, then local expert; stable in pair index),
+ *      writes send_rows [T*k][H] (bf16 token rows in that order),
+ *      send_local [T*k] (int64 local expert of each row) and slot_counts
+ *      [num_experts] (rows per slot; rows for rank r are the slots
+ *      r*experts_per_rank .. (r+1)*experts_per_rank-1).  The pair order is
+ *      kept in the handle for step 3.
+ *   2. moe_rows_forward on the expert's rank (handle whose weights are that
+ *      rank's experts_per_rank experts): y_rows[i] = fp32
+ *      down(silu(gate(x_i)) * up(x_i)) of local expert row_expert[i], for the
+ *      rows received from every rank, returned in the order received.
+ *   3. moe_ep_combine on the token's rank, same handle as step 1, after the
+ *      returned rows arrived in send order: out[t] = bf16(sum over slots j in
+ *      ascending expert order of w[t][j] * rows[pos(t, j)]), accumulated in
+ *      fp32 (nano_ktrans/kernels/cpu_moe.py:515-538 order).
+ * Expert ids outside [0, num_experts) are flagged in the status word and
+ * dropped, as in moe_experts_forward. */
+int moe_ep_dispatch(void* handle, const uint16_t* x_dev, const int64_t* topk_ids_dev, int32_t num_tokens,
+                    const int32_t* slot_of_expert_dev, int32_t experts_per_rank, int32_t world,
+                    uint16_t* send_rows_dev, int64_t* send_local_dev, int32_t* slot_counts_dev, void* stream);
+/* num_rows <= max_tokens * top_k of the handle. */
+int moe_rows_forward(void* handle, const uint16_t* x_rows_dev, const int64_t* row_expert_dev, int32_t num_rows,
+                     float* y_rows_dev, void* stream);
+int moe_ep_combine(void* handle, const int64_t* topk_ids_dev, const uint16_t* topk_weights_dev, int32_t num_tokens,
+                   const float* returned_rows_dev, uint16_t* out_dev, void* stream);
+
 /* Dequantize rows [row0, row0+nrows) of projection `proj` (0 gate, 1 up,
  * 2 down, 3..5 shared gate/up/down) of expert `expert` into fp32 [nrows, K],
  * with the same unpack code the matvec kernels use. */

@@ -61,6 +61,9 @@ SIGNATURES = {
     "moe_destroy": (None, [_vp]),
     "moe_decode_noalloc": (_i32, [ctypes.POINTER(MoeLayerDesc), ctypes.POINTER(MoeWeights), _vp, _vp, _i32, _vp, _vp,
                                   _vp, _vp, _vp, _cp, _sz]),
+    "moe_ep_dispatch": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "moe_rows_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "moe_ep_combine": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp]),
 }
 
 _lib = None

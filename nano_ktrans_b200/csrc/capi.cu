@@ -54,6 +54,7 @@ struct Handle {
   // shared expert on the GEMM path
   bool shared_gemm_maps = false;
   int32_t* sh_tables = nullptr;             // int32[6]: one-expert tables over T tokens
+  int64_t* slot_ids = nullptr;              // [max_pairs] expert-parallel slot of each pair (moe_ep_dispatch)
   alignas(64) unsigned char tm_sx[128];     // fp16 [max_tokens][H] over sh_y
   alignas(64) unsigned char tm_sh[128];     // fp16 [max_tokens][S] over sh_h
   alignas(64) unsigned char tm_sgate[128];  // uint8 [S][H*bits/8]
@@ -183,10 +184,10 @@ bool encode_gemm_maps(Handle* h) {
 
 // The GEMM path pays off once experts see several tokens each; below that
 // the matvec kernels stream the same weight bytes with less fixed cost.
-bool use_gemm(const Handle* h, int T) {
+bool use_gemm(const Handle* h, int pairs) {
   if (!h->gemm_maps || h->gemm_mode == 0) return false;
   if (h->gemm_mode == 2) return true;
-  return static_cast<int64_t>(T) * h->d.top_k >= 4LL * h->d.num_experts;
+  return pairs >= 4 * h->d.num_experts;
 }
 
 }  // namespace
@@ -221,7 +222,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
                o_nact = take(4), o_sorted = take(4 * P), o_pos = take(4 * P), o_h = take(4 * P * I),
                o_y = take(4 * P * H), o_shh = take(S ? 4 * T * S : 0), o_shy = take(S ? 4 * T * H : 0),
                o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P), o_bar = take(8),
-               o_tiles = take(4 * (E + 1)), o_shtab = take(4 * 8);
+               o_tiles = take(4 * (E + 1)), o_shtab = take(4 * 8), o_gids = take(8 * P);
   h->ws_bytes = off;
   cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
   if (e != cudaSuccess) {
@@ -249,6 +250,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   h->grid_bar = reinterpret_cast<unsigned long long*>(b + o_bar);
   h->tile_off = reinterpret_cast<int32_t*>(b + o_tiles);
   h->sh_tables = reinterpret_cast<int32_t*>(b + o_shtab);
+  h->slot_ids = reinterpret_cast<int64_t*>(b + o_gids);
   e = cudaMemset(h->ws, 0, h->ws_bytes);
   if (e != cudaSuccess) {
     fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
@@ -348,11 +350,19 @@ static bool try_decode_fused(Handle* h, const uint16_t* x, const uint16_t* logit
   return true;
 }
 
+// Routed experts for T tokens with `ids` [T][k].  Normally ends with the
+// weighted combine into `out`; with rows_out set, k is 1 (each "token" is one
+// (token, expert) row), the shared expert is skipped and the unweighted fp32
+// expert output of row r goes to rows_out[r].
 static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, const uint16_t* wts, int T,
-                           const uint8_t* mask, bool add_shared, uint16_t* out, cudaStream_t st, int launches) {
+                           const uint8_t* mask, bool add_shared, uint16_t* out, cudaStream_t st, int launches,
+                           float* rows_out = nullptr) {
   const moe_layer_desc& d = h->d;
-  const int E = d.num_experts, H = d.hidden_size, I = d.inter_size, k = d.top_k;
-  if (launches == 0 && try_decode_fused(h, x, nullptr, ids, wts, nullptr, nullptr, T, mask, add_shared, out, st))
+  const int E = d.num_experts, H = d.hidden_size, I = d.inter_size;
+  const int k = rows_out ? 1 : d.top_k;
+  if (rows_out) add_shared = false;
+  if (launches == 0 && !rows_out &&
+      try_decode_fused(h, x, nullptr, ids, wts, nullptr, nullptr, T, mask, add_shared, out, st))
     return check_launch(h, "moe_experts_forward");
   prof_mark(h, MOE_K_PERMUTE, false, st);
   moe::launch_permute(ids, T, k, E, mask, h->rt, st);
@@ -366,7 +376,7 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     return fail(h, MOE_EINVAL, "GEMM path forced but this layer's shape is outside its rules");
   const bool shared_gemm = add_shared && d.shared_inter > 0 && h->shared_gemm_maps && h->gemm_mode != 0 &&
                            (h->gemm_mode == 2 || T >= 16);
-  const bool routed_gemm = use_gemm(h, T);
+  const bool routed_gemm = use_gemm(h, T * k);
   if (routed_gemm || shared_gemm) {
     moe::launch_tile_table(h->rt, h->tile_off, shared_gemm ? h->sh_tables : nullptr, T, st);
     ++launches;
@@ -456,11 +466,14 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     sy = h->sh_y;
   }
   prof_mark(h, MOE_K_COMBINE, false, st);
-  moe::launch_combine(ids, wts, h->rt, T, k, H, h->ybuf, sg, sy, out, st);
+  if (rows_out)
+    moe::launch_scatter_rows(h->rt.pair_pos, T, H, h->ybuf, rows_out, h->num_sms, st);
+  else
+    moe::launch_combine(ids, wts, h->rt, T, k, H, h->ybuf, sg, sy, out, st);
   prof_mark(h, MOE_K_COMBINE, true, st);
   ++launches;
   h->last_launches = launches;
-  return check_launch(h, "moe_experts_forward");
+  return check_launch(h, rows_out ? "moe_rows_forward" : "moe_experts_forward");
 }
 
 static int check_forward_args(Handle* h, const void* x, const void* out, int T) {
@@ -501,6 +514,70 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
                     h->d.normalize_topk_prob != 0, ids, wts, st);
   prof_mark(h, MOE_K_ROUTE, true, st);
   return experts_forward(h, x_dev, ids, wts, T, nullptr, true, out_dev, st, 1);
+}
+
+int moe_ep_dispatch(void* handle, const uint16_t* x_dev, const int64_t* ids_dev, int32_t T,
+                    const int32_t* slot_of_expert_dev, int32_t experts_per_rank, int32_t world,
+                    uint16_t* send_rows_dev, int64_t* send_local_dev, int32_t* slot_counts_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  const moe_layer_desc& d = h->d;
+  if (T < 0) return fail(h, MOE_EINVAL, "moe_ep_dispatch: negative token count");
+  if (T > d.max_tokens) return fail(h, MOE_ERANGE, "moe_ep_dispatch: token count %d above max_tokens %d", T,
+                                    d.max_tokens);
+  if (world < 1 || experts_per_rank < 1 || static_cast<int64_t>(world) * experts_per_rank != d.num_experts)
+    return fail(h, MOE_EINVAL, "moe_ep_dispatch: world * experts_per_rank must equal num_experts");
+  if (slot_counts_dev == nullptr || slot_of_expert_dev == nullptr)
+    return fail(h, MOE_EINVAL, "moe_ep_dispatch: null table pointer");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int E = d.num_experts, k = d.top_k, P = T * d.top_k;
+  if (T > 0) {
+    if (x_dev == nullptr || ids_dev == nullptr || send_rows_dev == nullptr || send_local_dev == nullptr)
+      return fail(h, MOE_EINVAL, "moe_ep_dispatch: null device pointer");
+    moe::launch_ep_remap(ids_dev, P, slot_of_expert_dev, E, E, h->slot_ids, st);
+    moe::launch_permute(h->slot_ids, T, k, E, nullptr, h->rt, st);
+    moe::launch_ep_gather(x_dev, h->rt, E, h->slot_ids, k, d.hidden_size, experts_per_rank, P, send_rows_dev,
+                          send_local_dev, h->num_sms, st);
+    if (cudaMemcpyAsync(slot_counts_dev, h->rt.counts, sizeof(int32_t) * E, cudaMemcpyDeviceToDevice, st) !=
+        cudaSuccess)
+      return fail(h, MOE_ECUDA, "moe_ep_dispatch: counts copy failed");
+  } else if (cudaMemsetAsync(slot_counts_dev, 0, sizeof(int32_t) * E, st) != cudaSuccess) {
+    return fail(h, MOE_ECUDA, "moe_ep_dispatch: counts reset failed");
+  }
+  h->last_launches = T > 0 ? 3 : 0;
+  return check_launch(h, "moe_ep_dispatch");
+}
+
+int moe_rows_forward(void* handle, const uint16_t* x_rows_dev, const int64_t* row_expert_dev, int32_t n,
+                     float* y_rows_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (!h->has_weights) return fail(h, MOE_ENOWEIGHTS, "weights not set (call moe_set_weights first)");
+  if (n < 0) return fail(h, MOE_EINVAL, "moe_rows_forward: negative row count");
+  if (static_cast<int64_t>(n) > static_cast<int64_t>(h->d.max_tokens) * h->d.top_k)
+    return fail(h, MOE_ERANGE, "moe_rows_forward: %d rows above max_tokens * top_k = %d", n,
+                h->d.max_tokens * h->d.top_k);
+  h->last_launches = 0;
+  if (n == 0) return MOE_OK;
+  if (x_rows_dev == nullptr || row_expert_dev == nullptr || y_rows_dev == nullptr)
+    return fail(h, MOE_EINVAL, "moe_rows_forward: null device pointer");
+  return experts_forward(h, x_rows_dev, row_expert_dev, nullptr, n, nullptr, false, nullptr,
+                         static_cast<cudaStream_t>(stream), 0, y_rows_dev);
+}
+
+int moe_ep_combine(void* handle, const int64_t* ids_dev, const uint16_t* w_dev, int32_t T, const float* rows_dev,
+                   uint16_t* out_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (T < 0 || T > h->d.max_tokens) return fail(h, MOE_ERANGE, "moe_ep_combine: bad token count %d", T);
+  h->last_launches = 0;
+  if (T == 0) return MOE_OK;
+  if (ids_dev == nullptr || w_dev == nullptr || rows_dev == nullptr || out_dev == nullptr)
+    return fail(h, MOE_EINVAL, "moe_ep_combine: null device pointer");
+  moe::launch_combine(ids_dev, w_dev, h->rt, T, h->d.top_k, h->d.hidden_size, rows_dev, nullptr, nullptr, out_dev,
+                      static_cast<cudaStream_t>(stream));
+  h->last_launches = 1;
+  return check_launch(h, "moe_ep_combine");
 }
 
 int moe_dequant_rows(void* handle, int32_t proj, int32_t expert, int32_t row0, int32_t nrows, float* out_dev,

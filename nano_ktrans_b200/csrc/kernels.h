@@ -115,4 +115,16 @@ void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, in
 // 1 = launched, negative = refused (shared-memory opt-in failed).
 int launch_grouped_gemm(int bits, bool gateup, const GemmLaunch& g, cudaStream_t st);
 
+// ---- expert parallelism (ep.cu) ----
+// g[p] = slot_of_expert[ids[p]] (ids outside [0, E) -> num_slots).
+void launch_ep_remap(const int64_t* ids, int P, const int32_t* slot_of_expert, int E, int num_slots, int64_t* g,
+                     cudaStream_t st);
+// send_rows[s] = x[token of sorted pair s], send_local[s] = g % experts_per_rank.
+void launch_ep_gather(const uint16_t* x, const RouteTables& rt, int num_slots, const int64_t* g, int top_k, int H,
+                      int experts_per_rank, int max_pairs, uint16_t* send_rows, int64_t* send_local, int num_sms,
+                      cudaStream_t st);
+// rows[r] = y[pos[r]] (zero where pos[r] < 0).
+void launch_scatter_rows(const int32_t* pos, int n, int H, const float* y, float* rows, int num_sms,
+                         cudaStream_t st);
+
 }  // namespace moe
