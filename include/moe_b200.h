@@ -207,7 +207,11 @@ enum moe_option {
    * The GEMM path needs inter and hidden multiples of 128 and, for W4,
    * group_size a multiple of 64 (W8: per-channel); value 2 on another shape
    * is refused. */
-  MOE_OPT_GEMM = 3
+  MOE_OPT_GEMM = 3,
+  /* Token-tile width of the grouped GEMM: 0 (default) = the smallest of
+   * 16/32/64/128 covering the mean tokens per routed expert; or one of those
+   * four values. */
+  MOE_OPT_GEMM_TILE = 4
 };
 
 /* Copy the phase timestamps of the last traced single-launch decode step:

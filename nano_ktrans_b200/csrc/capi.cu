@@ -45,9 +45,11 @@ struct Handle {
   // prefill GEMM path: tensor maps over the activation buffers and the codes
   int32_t* tile_off = nullptr;  // [E+1]
   int gemm_mode = 1;            // 0 never, 1 by batch size, 2 whenever the shape allows
+  int gemm_tile = 0;            // token-tile width of the GEMM launches: 0 by batch, else 16/32/64/128
   bool gemm_maps = false;       // tensor maps encoded (shape supported, driver entry point found)
-  alignas(64) unsigned char tm_x[128];     // fp16 [max_pairs][H] over ybuf (x packed in pair order)
-  alignas(64) unsigned char tm_h[128];     // fp16 [max_pairs][I] over hbuf (SiLU(g)*u)
+  // activation maps, one per token-tile width 16 << i
+  alignas(64) unsigned char tm_x[moe::kGemmTileWidths][128];  // fp16 [max_pairs][H] over ybuf (x in pair order)
+  alignas(64) unsigned char tm_h[moe::kGemmTileWidths][128];  // fp16 [max_pairs][I] over hbuf (SiLU(g)*u)
   alignas(64) unsigned char tm_gate[128];  // uint8 [E*I][H*bits/8]
   alignas(64) unsigned char tm_up[128];
   alignas(64) unsigned char tm_down[128];  // uint8 [E*H][I*bits/8]
@@ -55,8 +57,8 @@ struct Handle {
   bool shared_gemm_maps = false;
   int32_t* sh_tables = nullptr;             // int32[6]: one-expert tables over T tokens
   int64_t* slot_ids = nullptr;              // [max_pairs] expert-parallel slot of each pair (moe_ep_dispatch)
-  alignas(64) unsigned char tm_sx[128];     // fp16 [max_tokens][H] over sh_y
-  alignas(64) unsigned char tm_sh[128];     // fp16 [max_tokens][S] over sh_h
+  alignas(64) unsigned char tm_sx[moe::kGemmTileWidths][128];  // fp16 [max_tokens][H] over sh_y
+  alignas(64) unsigned char tm_sh[moe::kGemmTileWidths][128];  // fp16 [max_tokens][S] over sh_h
   alignas(64) unsigned char tm_sgate[128];  // uint8 [S][H*bits/8]
   alignas(64) unsigned char tm_sup[128];
   alignas(64) unsigned char tm_sdown[128];  // uint8 [H][S*bits/8]
@@ -154,8 +156,11 @@ bool encode_gemm_maps(Handle* h) {
   const QuantProj down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
   if (!moe::gemm_shape_ok(bits, gate) || !moe::gemm_shape_ok(bits, down)) return false;
   const uint32_t code_box = moe::kGemmBK * bits / 8;
-  bool ok = moe::make_tmap_2d(h->tm_x, h->ybuf, true, H, P, moe::kGemmBK, moe::kGemmBN, true);
-  ok = ok && moe::make_tmap_2d(h->tm_h, h->hbuf, true, I, P, moe::kGemmBK, moe::kGemmBN, true);
+  bool ok = true;
+  for (int i = 0; i < moe::kGemmTileWidths; ++i) {
+    ok = ok && moe::make_tmap_2d(h->tm_x[i], h->ybuf, true, H, P, moe::kGemmBK, 16u << i, true);
+    ok = ok && moe::make_tmap_2d(h->tm_h[i], h->hbuf, true, I, P, moe::kGemmBK, 16u << i, true);
+  }
   ok = ok && moe::make_tmap_2d(h->tm_gate, h->w.gate_q_dev, false, static_cast<uint64_t>(H) * bits / 8,
                                static_cast<uint64_t>(E) * I, code_box, moe::kGemmBM, false);
   ok = ok && moe::make_tmap_2d(h->tm_up, h->w.up_q_dev, false, static_cast<uint64_t>(H) * bits / 8,
@@ -169,8 +174,10 @@ bool encode_gemm_maps(Handle* h) {
     const QuantProj sd = make_proj(h, h->w.shared_down_q_dev, h->w.shared_down_s_dev, H, S);
     const uint64_t T = static_cast<uint64_t>(d.max_tokens);
     bool sok = moe::gemm_shape_ok(bits, sg) && moe::gemm_shape_ok(bits, sd);
-    sok = sok && moe::make_tmap_2d(h->tm_sx, h->sh_y, true, H, T, moe::kGemmBK, moe::kGemmBN, true);
-    sok = sok && moe::make_tmap_2d(h->tm_sh, h->sh_h, true, S, T, moe::kGemmBK, moe::kGemmBN, true);
+    for (int i = 0; i < moe::kGemmTileWidths; ++i) {
+      sok = sok && moe::make_tmap_2d(h->tm_sx[i], h->sh_y, true, H, T, moe::kGemmBK, 16u << i, true);
+      sok = sok && moe::make_tmap_2d(h->tm_sh[i], h->sh_h, true, S, T, moe::kGemmBK, 16u << i, true);
+    }
     sok = sok && moe::make_tmap_2d(h->tm_sgate, h->w.shared_gate_q_dev, false, static_cast<uint64_t>(H) * bits / 8,
                                    S, code_box, moe::kGemmBM, false);
     sok = sok && moe::make_tmap_2d(h->tm_sup, h->w.shared_up_q_dev, false, static_cast<uint64_t>(H) * bits / 8, S,
@@ -184,6 +191,14 @@ bool encode_gemm_maps(Handle* h) {
 
 // The GEMM path pays off once experts see several tokens each; below that
 // the matvec kernels stream the same weight bytes with less fixed cost.
+// Token-tile width of a grouped-GEMM launch: the smallest of 16/32/64/128
+// covering the mean token count of an active expert.
+int pick_bn(int pairs, int experts) {
+  const int active = std::max(1, std::min(experts, pairs));
+  const int mean = (pairs + active - 1) / active;
+  return mean <= 16 ? 16 : mean <= 32 ? 32 : mean <= 64 ? 64 : 128;
+}
+
 bool use_gemm(const Handle* h, int pairs) {
   if (!h->gemm_maps || h->gemm_mode == 0) return false;
   if (h->gemm_mode == 2) return true;
@@ -377,8 +392,10 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
   const bool shared_gemm = add_shared && d.shared_inter > 0 && h->shared_gemm_maps && h->gemm_mode != 0 &&
                            (h->gemm_mode == 2 || T >= 16);
   const bool routed_gemm = use_gemm(h, T * k);
+  const int bn = h->gemm_tile ? h->gemm_tile : pick_bn(T * k, E);
+  const int sbn = h->gemm_tile ? h->gemm_tile : pick_bn(T, 1);
   if (routed_gemm || shared_gemm) {
-    moe::launch_tile_table(h->rt, h->tile_off, shared_gemm ? h->sh_tables : nullptr, T, st);
+    moe::launch_tile_table(h->rt, h->tile_off, shared_gemm ? h->sh_tables : nullptr, T, bn, sbn, st);
     ++launches;
   }
   if (routed_gemm) {
@@ -390,9 +407,10 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     g.status = h->rt.status;
     g.max_pairs = T * k;
     g.max_active = max_active;
+    g.bn = bn;
     g.p0 = gate;
     g.p1 = up;
-    g.tmap_x = h->tm_x;
+    g.tmap_x = h->tm_x[moe::gemm_tile_index(bn)];
     g.tmap_w0 = h->tm_gate;
     g.tmap_w1 = h->tm_up;
     g.hout = h->hbuf;
@@ -402,7 +420,7 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (gate/up): shared-memory opt-in refused");
     g.p0 = down;
     g.p1 = down;
-    g.tmap_x = h->tm_h;
+    g.tmap_x = h->tm_h[moe::gemm_tile_index(bn)];
     g.tmap_w0 = h->tm_down;
     g.tmap_w1 = h->tm_down;
     g.hout = nullptr;
@@ -440,9 +458,10 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
       g.status = h->rt.status;
       g.max_pairs = T;
       g.max_active = 1;
+      g.bn = sbn;
       g.p0 = sgp;
       g.p1 = sup;
-      g.tmap_x = h->tm_sx;
+      g.tmap_x = h->tm_sx[moe::gemm_tile_index(sbn)];
       g.tmap_w0 = h->tm_sgate;
       g.tmap_w1 = h->tm_sup;
       g.hout = h->sh_h;
@@ -450,7 +469,7 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
       if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (shared gate/up): shared-memory opt-in refused");
       g.p0 = sdp;
       g.p1 = sdp;
-      g.tmap_x = h->tm_sh;
+      g.tmap_x = h->tm_sh[moe::gemm_tile_index(sbn)];
       g.tmap_w0 = h->tm_sdown;
       g.tmap_w1 = h->tm_sdown;
       g.hout = nullptr;
@@ -632,6 +651,11 @@ int moe_set_option(void* handle, int32_t option, int32_t value) {
       if (value == 2 && h->has_weights && !h->gemm_maps)
         return fail(h, MOE_EINVAL, "moe_set_option(gemm): this layer's shape is outside the GEMM path's rules");
       h->gemm_mode = value;
+      return MOE_OK;
+    case MOE_OPT_GEMM_TILE:
+      if (value != 0 && value != 16 && value != 32 && value != 64 && value != 128)
+        return fail(h, MOE_EINVAL, "moe_set_option(gemm tile): value must be 0, 16, 32, 64 or 128");
+      h->gemm_tile = value;
       return MOE_OK;
     case MOE_OPT_TRACE:
       if (value && h->trace == nullptr) {

@@ -41,7 +41,6 @@ namespace moe {
 namespace gg {
 
 constexpr int BM = kGemmBM;  // weight rows per tile
-constexpr int BN = kGemmBN;  // tokens per tile
 constexpr int BK = kGemmBK;  // K per stage (one 128-byte fp16 row)
 constexpr uint32_t kSpin = 1u << 22;  // bounded waits: the kernel records kStatusTimeout and unwinds
 
@@ -108,13 +107,17 @@ MOE_DEV uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // kind::f16 instruction descriptor: D f32, A f16, B f16, both K-major, M x N.
-constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+template <int N>
+constexpr uint32_t idesc_f16() {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+}
 
+template <int N>
 MOE_DEV void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+      "l"(da), "l"(db), "r"(idesc_f16<N>()), "r"(accumulate)
       : "memory");
 }
 
@@ -201,7 +204,7 @@ struct GemmArgs {
 //   operand ring (2 stages): dequantized weight tile(s) [BM][64] fp16, written by the dequant warps.
 // A load stage is released when the MMAs that read it complete, which is after
 // the dequant warps consumed its codes (the MMAs wait for their operands).
-template <int BITS, bool GATEUP>
+template <int BITS, bool GATEUP, int BN>
 struct Plan {
   static constexpr int kCodeRow = BK * BITS / 8;  // code bytes per row per stage
   static constexpr int kNP = GATEUP ? 2 : 1;
@@ -213,11 +216,12 @@ struct Plan {
   static constexpr int kOS = 2;
   static constexpr int kBudget = 232448 - 2048;   // opt-in limit minus barriers and alignment slack
   static constexpr int kLSraw = (kBudget - kOS * kOper) / kLoad;
-  static constexpr int kLS = kLSraw > 8 ? 8 : kLSraw;
+  static constexpr int kLS = kLSraw > 12 ? 12 : kLSraw;
   static constexpr int kOperOff = kLS * kLoad;    // multiple of 1024
   static constexpr int kBarOff = kOperOff + kOS * kOper;
   static constexpr int kNumBars = 2 * kLS + 2 * kOS + 1;
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;
+  static constexpr int kTmemCols = kNP * BN < 32 ? 32 : kNP * BN;  // allocation: power of two >= 32
   static_assert(kLS >= 3, "load ring too shallow");
   static_assert(kLoad % 1024 == 0 && kOper % 1024 == 0, "tiles must stay 1024-byte aligned");
   static_assert(kBytes <= 232448, "shared-memory plan exceeds the opt-in limit");
@@ -226,11 +230,11 @@ struct Plan {
 constexpr int kDqWarps = 8;                         // dequant + epilogue warps (2 per TMEM lane quarter)
 constexpr int kThreadsV2 = 64 + 32 * kDqWarps;      // + producer warp + MMA warp
 
-template <int BITS, bool GATEUP>
+template <int BITS, bool GATEUP, int BN>
 __global__ void __launch_bounds__(kThreadsV2, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w0,
                         const __grid_constant__ CUtensorMap tm_w1, GemmArgs a) {
-  using L = Plan<BITS, GATEUP>;
+  using L = Plan<BITS, GATEUP, BN>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
   }
   if (warp == 1) {  // TMEM: kNP accumulators of BN fp32 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(L::kNP * BN));
+                 "r"(L::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -346,8 +350,8 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
-          umma_f16(tmem, da0 + 2 * kk, db + 2 * kk, acc);  // +32 bytes per K step of 16
-          if constexpr (GATEUP) umma_f16(tmem + BN, da1 + 2 * kk, db + 2 * kk, acc);
+          umma_f16<BN>(tmem, da0 + 2 * kk, db + 2 * kk, acc);  // +32 bytes per K step of 16
+          if constexpr (GATEUP) umma_f16<BN>(tmem + BN, da1 + 2 * kk, db + 2 * kk, acc);
         }
         umma_commit(smem_u32(&load_empty[s]));
         umma_commit(smem_u32(&oper_empty[o]));
@@ -414,10 +418,12 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
         if constexpr (GATEUP) s1w = bf16_to_f32(__ldg(a.s1 + srow));
       }
       const int col = GATEUP ? (row & ~7) + kpos<BITS>(row & 7) : row;
-      const int n0 = half * (BN / 2);
-      for (int j = 0; j < BN / 32; ++j) {
+      // token columns per warp half: 16-column loads, so a 16-wide tile uses one half only
+      constexpr int kHalfCols = BN / 2 < 16 ? 16 : BN / 2;
+      const int n0 = half * kHalfCols;
+      for (int j = 0; j < kHalfCols / 16; ++j) {
         const int nb = n0 + j * 16;
-        if (nb >= ntok) break;  // warp-uniform
+        if (nb >= ntok || nb >= BN) break;  // warp-uniform
         float d0[16], d1[16];
         tmem_ld16(tl + nb, d0);
         if constexpr (GATEUP) tmem_ld16(tl + BN + nb, d1);
@@ -440,7 +446,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::kNP * BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::kTmemCols));
   }
 #ifdef MOE_GEMM_TRACE
   if (tid == 0) {
@@ -453,13 +459,14 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
 #endif
 }
 
-// Token-tile prefix over the active experts: tile_off[a] = sum_{a' < a} ceil(count / BN).
+// Token-tile prefix over the active experts: tile_off[a] = sum_{a' < a} ceil(count / BN),
+// BN the tile width of the routed launches (SBN: of the shared expert's).
 // With shared != nullptr also writes the one-expert tables of the shared
 // expert over tokens 0..T-1: offsets {0, T}, active {0}, n_active 1,
 // tile_off {0, ceil(T / BN)}.
 __global__ void tile_table_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                                   const int32_t* __restrict__ n_active, int32_t* __restrict__ tile_off,
-                                  int32_t* __restrict__ shared, int T) {
+                                  int32_t* __restrict__ shared, int T, int BN, int SBN) {
   if (threadIdx.x != 0) return;
   const int n = *n_active;
   int acc = 0;
@@ -475,7 +482,7 @@ __global__ void tile_table_kernel(const int32_t* __restrict__ offsets, const int
     shared[2] = 0;  // active
     shared[3] = 1;  // n_active
     shared[4] = 0;  // tile_off
-    shared[5] = (T + BN - 1) / BN;
+    shared[5] = (T + SBN - 1) / SBN;
   }
 }
 
@@ -549,8 +556,9 @@ bool gemm_shape_ok(int bits, const QuantProj& p) {
   return true;
 }
 
-void launch_tile_table(const RouteTables& rt, int32_t* tile_off, int32_t* shared_tables, int T, cudaStream_t st) {
-  gg::tile_table_kernel<<<1, 32, 0, st>>>(rt.offsets, rt.active, rt.n_active, tile_off, shared_tables, T);
+void launch_tile_table(const RouteTables& rt, int32_t* tile_off, int32_t* shared_tables, int T, int bn, int sbn,
+                       cudaStream_t st) {
+  gg::tile_table_kernel<<<1, 32, 0, st>>>(rt.offsets, rt.active, rt.n_active, tile_off, shared_tables, T, bn, sbn);
 }
 
 void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, int top_k, int identity_tokens, int H,
@@ -565,10 +573,10 @@ void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, in
                                                 static_cast<__half*>(x16));
 }
 
-template <int BITS, bool GATEUP>
+template <int BITS, bool GATEUP, int BN>
 static int launch_gemm_t(const GemmLaunch& g, cudaStream_t st) {
-  using L = gg::Plan<BITS, GATEUP>;
-  auto kern = gg::grouped_gemm_kernel<BITS, GATEUP>;
+  using L = gg::Plan<BITS, GATEUP, BN>;
+  auto kern = gg::grouped_gemm_kernel<BITS, GATEUP, BN>;
   static int configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -590,7 +598,7 @@ static int launch_gemm_t(const GemmLaunch& g, cudaStream_t st) {
   a.hout = static_cast<__half*>(g.hout);
   a.yout = g.yout;
   a.status = g.status;
-  const int max_tiles = (g.max_pairs + gg::BN - 1) / gg::BN + g.max_active;
+  const int max_tiles = (g.max_pairs + BN - 1) / BN + g.max_active;
   const int grid = max_tiles * (g.p0.n / gg::BM);
   const CUtensorMap* tx = reinterpret_cast<const CUtensorMap*>(g.tmap_x);
   const CUtensorMap* t0 = reinterpret_cast<const CUtensorMap*>(g.tmap_w0);
@@ -599,9 +607,20 @@ static int launch_gemm_t(const GemmLaunch& g, cudaStream_t st) {
   return 1;
 }
 
+template <int BITS, bool GATEUP>
+static int launch_gemm_bn(const GemmLaunch& g, cudaStream_t st) {
+  switch (g.bn) {
+    case 16: return launch_gemm_t<BITS, GATEUP, 16>(g, st);
+    case 32: return launch_gemm_t<BITS, GATEUP, 32>(g, st);
+    case 64: return launch_gemm_t<BITS, GATEUP, 64>(g, st);
+    case 128: return launch_gemm_t<BITS, GATEUP, 128>(g, st);
+    default: return -2;
+  }
+}
+
 int launch_grouped_gemm(int bits, bool gateup, const GemmLaunch& g, cudaStream_t st) {
-  if (bits == 4) return gateup ? launch_gemm_t<4, true>(g, st) : launch_gemm_t<4, false>(g, st);
-  return gateup ? launch_gemm_t<8, true>(g, st) : launch_gemm_t<8, false>(g, st);
+  if (bits == 4) return gateup ? launch_gemm_bn<4, true>(g, st) : launch_gemm_bn<4, false>(g, st);
+  return gateup ? launch_gemm_bn<8, true>(g, st) : launch_gemm_bn<8, false>(g, st);
 }
 
 }  // namespace moe

@@ -89,14 +89,17 @@ bool make_tmap_2d(void* out_map, const void* base, bool fp16, uint64_t inner, ui
 // Shape rules of the GEMM path for one projection (N % 128, K % 64, W4 group
 // % 64, W8 per-channel).
 bool gemm_shape_ok(int bits, const QuantProj& p);
-// Box sizes the tensor maps must be encoded with.
-constexpr int kGemmBM = 128, kGemmBN = 128, kGemmBK = 64;
+// Box sizes the tensor maps must be encoded with: codes {64*bits/8, kGemmBM},
+// activations {kGemmBK, bn} for the launch's token-tile width bn.
+constexpr int kGemmBM = 128, kGemmBK = 64;
+constexpr int kGemmTileWidths = 4;  // bn = 16 << i, i < kGemmTileWidths
+inline int gemm_tile_index(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : 3; }
 
 struct GemmLaunch {
   RouteTables rt;
   const int32_t* tile_off;  // [E+1] from launch_tile_table
   QuantProj p0, p1;         // gate, up (gate/up GEMM) or down, unused
-  const void* tmap_x;       // activations fp16 [rows][K], box {64, 128}, 128-byte swizzle
+  const void* tmap_x;       // activations fp16 [rows][K], box {64, bn}, 128-byte swizzle
   const void* tmap_w0;      // codes of p0 as uint8 [E*N][K*bits/8], box {64*bits/8, 128}
   const void* tmap_w1;      // codes of p1 (gate/up only)
   void* hout;               // gate/up: fp16 SiLU(g)*u [pairs][N], K-permuted for the down GEMM
@@ -104,11 +107,13 @@ struct GemmLaunch {
   int* status;
   int max_pairs;            // upper bound of the pair count of this call
   int max_active;           // upper bound of the active expert count of this call
+  int bn;                   // token-tile width: 16, 32, 64 or 128 (tile_off and tmap_x built for it)
 };
 // tile_off over the active experts; with shared_tables != nullptr also the
 // int32[6] one-expert tables of the shared expert over T tokens: offsets[2],
 // active[1], n_active[1], tile_off[2].
-void launch_tile_table(const RouteTables& rt, int32_t* tile_off, int32_t* shared_tables, int T, cudaStream_t st);
+void launch_tile_table(const RouteTables& rt, int32_t* tile_off, int32_t* shared_tables, int T, int bn, int sbn,
+                       cudaStream_t st);
 // x16[s] = fp16(x[token of sorted pair s]) with K permuted to the dequant order.
 void launch_pack_x(int bits, const uint16_t* x, const RouteTables& rt, int E, int top_k, int identity_tokens, int H,
                    int max_pairs, void* x16, int num_sms, cudaStream_t st);

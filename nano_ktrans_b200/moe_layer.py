@@ -156,6 +156,10 @@ class MoeLayer:
         grouped GEMM for large batches (default), 2 grouped GEMM for every batch."""
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_GEMM, int(mode)), self._h, "moe_set_option")
 
+    def set_gemm_tile(self, width: int) -> None:
+        """Token-tile width of the grouped GEMM: 0 chooses by batch, else 16, 32, 64 or 128."""
+        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_GEMM_TILE, int(width)), self._h, "moe_set_option")
+
     def set_trace(self, enabled: bool) -> None:
         """Record per-CTA phase timestamps in the single-launch decode kernel."""
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_TRACE, int(bool(enabled))), self._h, "moe_set_option")

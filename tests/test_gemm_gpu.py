@@ -50,19 +50,21 @@ def _weights(t, top_k, seed):
     return mo.f32_to_bf16_bits(w / w.sum(axis=1, keepdims=True))
 
 
-def _run(layer, x, ids, w, dev, mode, mask=None):
+def _run(layer, x, ids, w, dev, mode, mask=None, tile=0):
     layer.set_decode_fused(False)
     layer.set_gemm(mode)
+    layer.set_gemm_tile(tile)
     out = layer.experts_forward(hp.bf16_tensor(x, dev), torch.from_numpy(ids).to(dev), hp.bf16_tensor(w, dev),
                                 offload_mask=None if mask is None else torch.from_numpy(mask).to(dev))
     torch.cuda.synchronize()
     return hp.bf16_bits(out), layer.last_launch_count()
 
 
+@pytest.mark.parametrize("tile", [16, 32, 64, 128])
 @pytest.mark.parametrize("bits,group", [(4, 64), (4, 128), (4, 0), (8, 0)], ids=["w4g64", "w4g128", "w4pc", "w8pc"])
-def test_gemm_ragged_tiles(bits, group, cuda_device):
+def test_gemm_ragged_tiles(bits, group, tile, cuda_device):
     """Per-expert token counts 129, 128, 1, 0, 257, 6, 127 against the oracle,
-    and against the matvec path."""
+    and against the matvec path, at every token-tile width."""
     E, k, H, I = 7, 2, 256, 384
     counts = [129, 128, 1, 0, 257, 6, 127]
     ids = _ids_with_counts(counts, k, 11)
@@ -72,7 +74,7 @@ def test_gemm_ragged_tiles(bits, group, cuda_device):
     experts = {e: hp.make_expert(9, e, H, I, bits, group) for e in range(E) if counts[e]}
     lw = hp.device_layer(experts, E, H, I, bits, group, cuda_device)
     layer = _layer(lw, k, max_tokens=t)
-    got, n = _run(layer, x, ids, w, cuda_device, 2)
+    got, n = _run(layer, x, ids, w, cuda_device, 2, tile=tile)
     assert n == GEMM_LAUNCHES
     ref = mo.offload_forward_f32(x, ids, w, experts)
     hp.assert_parity(got, ref, MAX_ABS, MEAN_REL)
@@ -111,6 +113,10 @@ def test_gemm_deterministic(cuda_device):
     a, _ = _run(layer, x, ids, w, cuda_device, 2)
     b, _ = _run(layer, x, ids, w, cuda_device, 2)
     assert np.array_equal(a, b)
+    # the tile width changes which tokens share an MMA, not any token's arithmetic
+    for tile in (16, 32, 64, 128):
+        c, _ = _run(layer, x, ids, w, cuda_device, 2, tile=tile)
+        assert np.array_equal(a, c), tile
 
 
 @pytest.mark.parametrize("tokens", [64, 256])
