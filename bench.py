@@ -61,6 +61,10 @@ def parse_args():
     ap.add_argument("--prefill", default="mixtral,qwen2",
                     help="prefill workloads to report beside the decode line: mixtral (config 3), qwen2 (config 4)")
     ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--ep", default="4096,64",
+                    help="config 5: global prefill,decode token counts of the 48-layer expert-parallel stack "
+                         "('' = skip)")
+    ap.add_argument("--ep-steps", type=int, default=3)
     ap.add_argument("--skip-decode", action="store_true",
                     help="report only the prefill workloads (profiling runs of the grouped GEMM)")
     return ap.parse_args()
@@ -553,6 +557,8 @@ def main():
     pre = prefill_block(args, dev, rank)
     if pre:
         line["prefill"] = pre
+    if args.ep:
+        line["ep"] = run_ep(args, world, rank, dev, uniq, lws)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, n, busy = cpu_reference_rate(lws, x, logits, args.cpu_seconds, 10 ** 6)
@@ -712,6 +718,103 @@ def prefill_block(args, dev, rank):
         r["replicas"] = world
         out[name] = r
     return out
+
+
+# ---------------------------------------------------------------------------
+# config 5: 48-layer stack, experts split across the ranks
+# ---------------------------------------------------------------------------
+
+
+def run_ep(args, world, rank, dev, uniq, lws):
+    """Config 5: the 48-layer Qwen3-shaped stack (W4 g128, Zipf(1.2) routing)
+    with each layer's 128 experts split over the ranks (frequency-balanced
+    placement, NCCL all-to-all dispatch and combine); global prefill and
+    decode batches split evenly over the ranks.  One GPU runs the same
+    layers through the single-GPU path.  Times are CUDA events around a
+    pass over all 48 layers (max over ranks)."""
+    import torch
+
+    from nano_ktrans_b200.expert_parallel import EpMoeLayer, TorchDistComm, plan_placement, shard_layer
+    from nano_ktrans_b200.moe_layer import MoeLayer
+
+    E, H, k = CFG["experts"], CFG["hidden"], CFG["top_k"]
+    n_prefill, n_decode = [int(v) for v in args.ep.split(",")]
+    L = len(lws)
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 5000)  # same router and bias on every rank
+    routers = [(torch.randn(E, H, generator=gen, device=dev) * 0.02).to(torch.bfloat16) for _ in range(L)]
+    biases = [zipf_router_bias(E, 1.2, gen, dev) for _ in range(L)]
+    tgen = torch.Generator(device=dev).manual_seed(args.seed + 6000 + rank)  # this rank's tokens
+
+    def batch(n_global):
+        t = n_global // world + (1 if rank < n_global % world else 0)
+        xs = [torch.randn(t, H, generator=tgen, device=dev).to(torch.bfloat16) for _ in range(L)]
+        lg = [((x @ r.T).float() + b).to(torch.bfloat16) for x, r, b in zip(xs, routers, biases)]
+        return t, xs, lg
+
+    tp, xp, lp = batch(n_prefill)
+    td, xd, ld = batch(n_decode)
+    res = {"placement": "frequency-balanced (prefill batch routing counts, all ranks)", "world": world,
+           "zipf_alpha": 1.2, "zipf_beta": 1.0}
+
+    if world == 1:
+        layers = [MoeLayer(lw, top_k=k, router_use_softmax=True, normalize_topk_prob=True, max_tokens=tp)
+                  for lw in lws]
+
+        def step(xs, lg):
+            for lay, x, g in zip(layers, xs, lg):
+                lay.forward(x, g)
+        res["path"] = "single GPU: moe_forward per layer (all experts local)"
+    else:
+        comm = TorchDistComm()
+        probe = EpMoeLayer(shard_layer(uniq[0], plan_placement(E, world), rank, world), num_experts=E, top_k=k,
+                           slot_of_expert=plan_placement(E, world), rank=rank, world=world, max_tokens=tp)
+        layers = []
+        max_ratio = 0.0
+        for i in range(L):
+            ids, _ = probe.route(lp[i])
+            freq = torch.bincount(ids.reshape(-1), minlength=E).to(torch.float64)
+            torch.distributed.all_reduce(freq)
+            slot = plan_placement(E, world, freq.cpu().numpy())
+            epr = E // world
+            loads = [0.0] * world
+            for e in range(E):
+                loads[int(slot[e]) // epr] += float(freq[e])
+            max_ratio = max(max_ratio, max(loads) / (sum(loads) / world))
+            layers.append(EpMoeLayer(shard_layer(uniq[i % len(uniq)], slot, rank, world), num_experts=E, top_k=k,
+                                     slot_of_expert=slot, rank=rank, world=world, max_tokens=max(tp, td)))
+        probe.close()
+        res["max_rank_load_over_mean"] = max_ratio
+
+        def step(xs, lg):
+            for lay, x, g in zip(layers, xs, lg):
+                lay.forward(x, g, comm)
+        res["path"] = ("expert parallel: moe_ep_dispatch -> NCCL all_to_all -> moe_rows_forward -> all_to_all "
+                       "-> moe_ep_combine")
+
+    def timed(xs, lg, steps):
+        step(xs, lg)  # warm-up pass
+        torch.cuda.synchronize()
+        if torch.distributed.is_initialized():
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step(xs, lg)
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    flops_layer = 2.0 * n_prefill * k * 3 * H * CFG["inter"]
+    ms = timed(xp, lp, args.ep_steps)
+    res["prefill"] = {"global_tokens": n_prefill, "ms_per_48_layers": ms, "tokens_per_s": n_prefill / (ms / 1e3),
+                      "routed_tflops": flops_layer * L / (ms / 1e3) / 1e12}
+    ms = timed(xd, ld, 3 * args.ep_steps)
+    res["decode"] = {"global_tokens": n_decode, "ms_per_48_layers": ms, "tokens_per_s": n_decode / (ms / 1e3)}
+    for lay in layers:
+        lay.close()
+    torch.cuda.empty_cache()
+    return res
 
 
 def read_traffic(kernel: str, batch: int):
