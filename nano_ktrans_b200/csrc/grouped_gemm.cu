@@ -1,17 +1,18 @@
 // grouped_gemm.cu — prefill path: per-expert grouped GEMM on tcgen05 tensor
-// cores with the weights dequantized in shared memory.
+// cores, the quantized weights dequantized on the fly into tensor memory.
 //
-// Replaces, for batches with many tokens per expert, the per-expert loop of
+// Replaces, for batches with several tokens per expert, the per-expert loop of
 // nano_ktrans/kernels/cpu_moe.py:515-536 (gate/up/down via the grouped W4A32
 // matvec, quantized_ops.py:86-124, SiLU(gate)*up at cpu_moe.py:448).
 //
 // Orientation ("swap AB"): the MMA's M = 128 weight rows (output features),
-// N = 128 tokens of one expert, K = the reduction dimension in steps of 64.
-//   A  (weights)     fp16, dequantized by CUDA cores from the W4/W8 codes into
-//                    a 128 x 64 K-major tile with the 128-byte swizzle;
+// N = 16..128 tokens of one expert (the token-tile width), K = the reduction
+// dimension in steps of 64.
+//   A  (weights)     fp16, dequantized by CUDA cores from the W4/W8 codes and
+//                    stored straight into tensor memory (tcgen05.st);
 //   B  (activations) fp16 [pairs, K] in expert-sorted pair order, loaded by
-//                    TMA (tensor map, 128-byte swizzle);
-//   D               fp32 in tensor memory (TMEM).
+//                    TMA (tensor map, 128-byte swizzle) into shared memory;
+//   D               fp32 in tensor memory.
 // Exactness: (q - z) * s has at most 3+8 (W4) significant bits, so it is
 // exact in fp16; W8 per-channel uses (q - 128) (exact) and applies the scale
 // in the epilogue.  Activations are bf16 inputs converted to fp16 (exact for
@@ -24,10 +25,11 @@
 // applied to both operands, so the activation buffers are written in that
 // same order (pack_x_kernel, and the gate/up epilogue for the down GEMM).
 //
-// CTA roles (192 threads): warp 0 issues the TMA loads; warp 1 owns TMEM and
-// one lane issues the MMAs; warps 2-5 (128 threads, thread = weight row)
-// dequantize, then run the epilogue from TMEM.  Stages are handed over with
-// mbarriers; every wait is bounded and records kStatusTimeout on expiry.
+// CTA roles (320 threads): warp 0 issues the TMA loads; warp 1 owns TMEM and
+// one lane issues the MMAs; warps 2-9 (two per TMEM lane quarter, thread =
+// weight row x half of the K step) dequantize, then run the epilogue from
+// TMEM.  Stages are handed over with mbarriers; every wait is bounded and
+// records kStatusTimeout on expiry.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -45,9 +47,9 @@ constexpr int BK = kGemmBK;  // K per stage (one 128-byte fp16 row)
 constexpr uint32_t kSpin = 1u << 22;  // bounded waits: the kernel records kStatusTimeout and unwinds
 
 #ifdef MOE_GEMM_TRACE
-// Instrumented builds only: per-CTA %globaltimer stamps of the last launch.
+// Instrumented builds only: per-CTA %globaltimer stamps and cycle sums of the last launch.
 constexpr int kTraceCtas = 1 << 15;
-__device__ unsigned long long g_gemm_trace[2][kTraceCtas][8];  // [down, gate/up][cta][stamp]
+__device__ unsigned long long g_gemm_trace[2][kTraceCtas][16];  // [down, gate/up][cta][stamp / cycle sum]
 template <bool GATEUP>
 MOE_DEV void stamp(int i) {
   if (blockIdx.x < kTraceCtas) {
@@ -57,8 +59,13 @@ MOE_DEV void stamp(int i) {
   }
 }
 #define GG_STAMP(i) stamp<GATEUP>(i)
+#define GG_SUM(i, v) \
+  if (blockIdx.x < kTraceCtas) g_gemm_trace[GATEUP ? 1 : 0][blockIdx.x][i] = static_cast<unsigned long long>(v)
+MOE_DEV long long gg_clock() { return clock64(); }
 #else
 #define GG_STAMP(i) ((void)0)
+#define GG_SUM(i, v) ((void)0)
+MOE_DEV long long gg_clock() { return 0; }
 #endif
 
 MOE_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -199,9 +206,16 @@ struct GemmArgs {
   int* status;
 };
 
-// Shared-memory plan.  Two rings:
-//   load ring  (kLS stages): activation tile [BN][64] fp16 + code tile(s) [BM][64*BITS/8], filled by TMA;
-//   operand ring (2 stages): dequantized weight tile(s) [BM][64] fp16, written by the dequant warps.
+// Operand staging.
+//   load ring (shared memory, kLS stages): activation tile [BN][64] fp16 and
+//     code tile(s) [BM][64*BITS/8], filled by TMA;
+//   operand ring (tensor memory, kOS stages): the dequantized weight tile(s)
+//     [BM][64] fp16, written by the dequant warps with tcgen05.st, one TMEM
+//     lane per weight row, two fp16 per 32-bit column along K (32 columns per
+//     projection per stage).  The MMAs read A from tensor memory and B from
+//     shared memory, so the dequantized weights never pass through shared
+//     memory.
+// Tensor memory: [accumulators kNP x BN columns][operand stages kOS x kNP x 32].
 // A load stage is released when the MMAs that read it complete, which is after
 // the dequant warps consumed its codes (the MMAs wait for their operands).
 template <int BITS, bool GATEUP, int BN>
@@ -210,25 +224,51 @@ struct Plan {
   static constexpr int kNP = GATEUP ? 2 : 1;
   static constexpr int kX = BN * 128;             // activation tile
   static constexpr int kC = BM * kCodeRow;        // code tile, per projection
-  static constexpr int kA = BM * 128;             // dequantized tile, per projection
   static constexpr int kLoad = kX + kNP * kC;
-  static constexpr int kOper = kNP * kA;
-  static constexpr int kOS = 2;
+  static constexpr int kACols = BK / 2;           // TMEM columns of one dequantized tile
+  static constexpr int kAccCols = kNP * BN;
+  // operand stages: as many as the 512 TMEM columns hold beside the accumulators (at most 12)
+  static constexpr int kOSraw = (512 - kAccCols) / (kNP * kACols);
+  static constexpr int kOS = kOSraw > 12 ? 12 : kOSraw;
+  static constexpr int kTmemUsed = kAccCols + kOS * kNP * kACols;
+  static constexpr int kTmemCols = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
+                                   : kTmemUsed <= 256 ? 256 : 512;  // allocation: power of two
   static constexpr int kBudget = 232448 - 2048;   // opt-in limit minus barriers and alignment slack
-  static constexpr int kLSraw = (kBudget - kOS * kOper) / kLoad;
-  static constexpr int kLS = kLSraw > 12 ? 12 : kLSraw;
-  static constexpr int kOperOff = kLS * kLoad;    // multiple of 1024
-  static constexpr int kBarOff = kOperOff + kOS * kOper;
+  static constexpr int kLSraw = kBudget / kLoad;
+  static constexpr int kLS = kLSraw > 16 ? 16 : kLSraw;
+  static constexpr int kBarOff = kLS * kLoad;
   static constexpr int kNumBars = 2 * kLS + 2 * kOS + 1;
-  static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;
-  static constexpr int kTmemCols = kNP * BN < 32 ? 32 : kNP * BN;  // allocation: power of two >= 32
-  static_assert(kLS >= 3, "load ring too shallow");
-  static_assert(kLoad % 1024 == 0 && kOper % 1024 == 0, "tiles must stay 1024-byte aligned");
+  // at least 116 KB of shared memory, so one CTA per SM holds the tensor memory it allocates
+  static constexpr int kBytesRaw = kBarOff + 8 * kNumBars + 16 + 1024;
+  static constexpr int kBytes = kBytesRaw < 118784 ? 118784 : kBytesRaw;
+  static_assert(kLS >= 4 && kOS >= 4, "rings too shallow");
+  static_assert(kTmemUsed <= 512, "tensor memory plan exceeds 512 columns");
+  static_assert(kLoad % 1024 == 0, "tiles must stay 1024-byte aligned");
   static_assert(kBytes <= 232448, "shared-memory plan exceeds the opt-in limit");
 };
 
 constexpr int kDqWarps = 8;                         // dequant + epilogue warps (2 per TMEM lane quarter)
 constexpr int kThreadsV2 = 64 + 32 * kDqWarps;      // + producer warp + MMA warp
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16, M = 128, N = BN.
+template <int N>
+MOE_DEV void umma_ts_f16(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc_f16<N>()), "r"(accumulate)
+      : "memory");
+}
+
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers.
+MOE_DEV void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 
 template <int BITS, bool GATEUP, int BN>
 __global__ void __launch_bounds__(kThreadsV2, 1)
@@ -262,11 +302,12 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
   const int wrow = e * a.N + fb * BM;  // first weight row (codes tensor row)
   const int nk = a.K / BK;
   if (tid == 0) GG_STAMP(0);
+  const long long cta_clock0 = gg_clock();
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* load_full = bars;                   // [kLS]  TMA bytes landed
   uint64_t* load_empty = bars + L::kLS;         // [kLS]  MMAs reading the stage completed
-  uint64_t* oper_full = bars + 2 * L::kLS;      // [kOS]  256 dequant threads wrote the operand
+  uint64_t* oper_full = bars + 2 * L::kLS;      // [kOS]  256 dequant threads stored the operand
   uint64_t* oper_empty = oper_full + L::kOS;    // [kOS]  MMAs reading the operand completed
   uint64_t* acc_full = oper_empty + L::kOS;     // [1]    last MMA completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
@@ -286,7 +327,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_flag = 0;
   }
-  if (warp == 1) {  // TMEM: kNP accumulators of BN fp32 columns
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(L::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -303,21 +344,25 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
       atomicOr(a.status, kStatusTimeout);
     }
   };
-  // load stage: X | C0 | C1 ; operand stage: A0 | A1
+  // load stage: X | C0 | C1
   auto x_tile = [&](int s) { return smem + s * L::kLoad; };
   auto c_tile = [&](int s, int p) { return smem + s * L::kLoad + L::kX + p * L::kC; };
-  auto a_tile = [&](int s, int p) { return smem + L::kOperOff + s * L::kOper + p * L::kA; };
+  // TMEM column of operand stage o, projection p
+  auto a_col = [&](int o, int p) { return static_cast<uint32_t>(L::kAccCols + (o * L::kNP + p) * L::kACols); };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int issued = 0;
+      long long w_empty = 0;
       for (int c = 0; c < nk && !*abort_flag; ++c) {
         const int s = c % L::kLS;
+        const long long t0 = gg_clock();
         if (c >= L::kLS && !mbar_wait(smem_u32(&load_empty[s]), static_cast<uint32_t>(((c / L::kLS) - 1) & 1))) {
           give_up();
           break;
         }
+        w_empty += gg_clock() - t0;
         const uint32_t full = smem_u32(&load_full[s]);
         mbar_expect_tx(full, static_cast<uint32_t>(L::kLoad));
         tma_load_2d(smem_u32(x_tile(s)), &tm_x, c * BK, s_begin, full);
@@ -326,6 +371,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
         issued = c + 1;
       }
       GG_STAMP(4);
+      GG_SUM(8, w_empty);
       if (*abort_flag) {
         // no copy may still be landing in shared memory when the CTA exits
         for (int c = max(0, issued - L::kLS); c < issued; ++c)
@@ -335,28 +381,37 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
+      long long w_of = 0, w_lf = 0, t_iss = 0;
       for (int c = 0; c < nk && !*abort_flag; ++c) {
         const int s = c % L::kLS, o = c % L::kOS;
-        if (!mbar_wait(smem_u32(&oper_full[o]), static_cast<uint32_t>((c / L::kOS) & 1)) ||
-            !mbar_wait(smem_u32(&load_full[s]), static_cast<uint32_t>((c / L::kLS) & 1))) {
+        const long long t0 = gg_clock();
+        const bool ok_o = mbar_wait(smem_u32(&oper_full[o]), static_cast<uint32_t>((c / L::kOS) & 1));
+        const long long t1 = gg_clock();
+        if (!ok_o || !mbar_wait(smem_u32(&load_full[s]), static_cast<uint32_t>((c / L::kLS) & 1))) {
           give_up();
           break;
         }
+        const long long t2 = gg_clock();
+        w_of += t1 - t0;
+        w_lf += t2 - t1;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (c == 0) GG_STAMP(2);
         const uint64_t db = sw128_desc(smem_u32(x_tile(s)));
-        const uint64_t da0 = sw128_desc(smem_u32(a_tile(o, 0)));
-        const uint64_t da1 = GATEUP ? sw128_desc(smem_u32(a_tile(o, 1))) : 0;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
-          umma_f16<BN>(tmem, da0 + 2 * kk, db + 2 * kk, acc);  // +32 bytes per K step of 16
-          if constexpr (GATEUP) umma_f16<BN>(tmem + BN, da1 + 2 * kk, db + 2 * kk, acc);
+          // A: 16 fp16 of K = 8 TMEM columns per step; B: +32 bytes per step
+          umma_ts_f16<BN>(tmem, tmem + a_col(o, 0) + 8 * kk, db + 2 * kk, acc);
+          if constexpr (GATEUP) umma_ts_f16<BN>(tmem + BN, tmem + a_col(o, 1) + 8 * kk, db + 2 * kk, acc);
         }
         umma_commit(smem_u32(&load_empty[s]));
         umma_commit(smem_u32(&oper_empty[o]));
+        t_iss += gg_clock() - t2;
       }
       GG_STAMP(3);
+      GG_SUM(9, w_of);
+      GG_SUM(10, w_lf);
+      GG_SUM(15, t_iss);
       umma_commit(smem_u32(acc_full));
       // every MMA has finished (normal or aborted) before TMEM is released
       if (!mbar_wait(smem_u32(acc_full), 0u)) give_up();
@@ -365,52 +420,83 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
     // ---------------- dequant (warps 2-9), then epilogue ----------------
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;        // which half of the K chunk / of the token columns
-    const int r = quarter * 32 + lane;       // weight row within the tile
+    const int r = quarter * 32 + lane;       // weight row within the tile = TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const size_t srow = static_cast<size_t>(wrow + r) * a.sstride;
+    constexpr int kVec = L::kCodeRow / 32;   // uint4 code vectors per half row (W4 1, W8 2)
+    constexpr int kOut = 4 / kVec;           // output uint4 per code vector
+    // W4 group scales: the next chunk's are loaded one chunk ahead
+    __half2 sc_cur[L::kNP], sc_next[L::kNP];
+#pragma unroll
+    for (int p = 0; p < L::kNP; ++p) {
+      sc_cur[p] = sc_next[p] = __float2half2_rn(1.0f);
+      if constexpr (BITS == 4)
+        sc_next[p] = __float2half2_rn(bf16_to_f32(__ldg((p == 0 ? a.s0 : a.s1) + srow)));
+    }
+    long long w_lf = 0, w_oe = 0, t_dq = 0;
     for (int c = 0; c < nk; ++c) {
       const int s = c % L::kLS, o = c % L::kOS;
-      if (*abort_flag) break;
-      if (!mbar_wait(smem_u32(&load_full[s]), static_cast<uint32_t>((c / L::kLS) & 1)) ||
-          (c >= L::kOS && !mbar_wait(smem_u32(&oper_empty[o]), static_cast<uint32_t>(((c / L::kOS) - 1) & 1)))) {
+      if (__any_sync(0xffffffffu, *abort_flag)) break;
+#pragma unroll
+      for (int p = 0; p < L::kNP; ++p) {
+        sc_cur[p] = sc_next[p];
+        if constexpr (BITS == 4) {
+          if (c + 1 < nk)
+            sc_next[p] = __float2half2_rn(bf16_to_f32(__ldg((p == 0 ? a.s0 : a.s1) + srow + ((c + 1) * BK) / a.group)));
+        }
+      }
+      const long long t0 = gg_clock();
+      const bool ok_l = mbar_wait(smem_u32(&load_full[s]), static_cast<uint32_t>((c / L::kLS) & 1));
+      const long long t1 = gg_clock();
+      const bool ok_o = ok_l && (c < L::kOS ||
+                                 mbar_wait(smem_u32(&oper_empty[o]), static_cast<uint32_t>(((c / L::kOS) - 1) & 1)));
+      if (!__all_sync(0xffffffffu, ok_o)) {
         give_up();
         break;
       }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const long long t2 = gg_clock();
+      w_lf += t1 - t0;
+      w_oe += t2 - t1;
 #pragma unroll
       for (int p = 0; p < L::kNP; ++p) {
-        __half2 sc = __float2half2_rn(1.0f);
-        if constexpr (BITS == 4) {
-          const uint16_t* sp = p == 0 ? a.s0 : a.s1;
-          sc = __float2half2_rn(bf16_to_f32(__ldg(sp + srow + (c * BK) / a.group)));
-        }
-        // this thread's half of the row: 16 code bytes (W4) or 32 (W8) -> output chunks 4*half .. 4*half+3
+        // this thread's half of the row: 16 code bytes (W4) or 32 (W8) -> 32 fp16 = 16 TMEM columns
         const uint4* codes = reinterpret_cast<const uint4*>(c_tile(s, p) + r * L::kCodeRow + half * (L::kCodeRow / 2));
-        unsigned char* arow = a_tile(o, p) + r * 128;
-        constexpr int kVec = L::kCodeRow / 32;  // uint4 code vectors per half row
-        constexpr int kOut = 4 / kVec;           // output chunks per code vector
+        uint32_t cols[16];
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
           uint4 ov[kOut];
-          dequant16<BITS>(codes[j], sc, ov);
+          dequant16<BITS>(codes[j], sc_cur[p], ov);
 #pragma unroll
           for (int q = 0; q < kOut; ++q) {
-            const int chunk = 4 * half + j * kOut + q;  // 16-byte chunk of the 128-byte row
-            *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = ov[q];
+            cols[(j * kOut + q) * 4 + 0] = ov[q].x;
+            cols[(j * kOut + q) * 4 + 1] = ov[q].y;
+            cols[(j * kOut + q) * 4 + 2] = ov[q].z;
+            cols[(j * kOut + q) * 4 + 3] = ov[q].w;
           }
         }
+        tmem_st16(tmem + lane_base + a_col(o, p) + half * 16, cols);
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(smem_u32(&oper_full[o]));
+      t_dq += gg_clock() - t2;
     }
-    // epilogue: this warp's 32 rows x 64 token columns
-    bool ok = !*abort_flag;
-    if (ok && !mbar_wait(smem_u32(acc_full), 0u)) {
+    if (warp == 2 && lane == 0) {
+      GG_SUM(11, w_lf);
+      GG_SUM(12, w_oe);
+      GG_SUM(13, t_dq);
+    }
+    // epilogue: this warp's 32 rows x up to 64 token columns
+    bool ok = !__any_sync(0xffffffffu, *abort_flag);
+    if (ok && !__all_sync(0xffffffffu, mbar_wait(smem_u32(acc_full), 0u))) {
       give_up();
       ok = false;
     }
-    if (ok && !*abort_flag) {
+    if (ok) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       if (warp == 2 && lane == 0) GG_STAMP(5);
-      const uint32_t tl = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      const uint32_t tl = tmem + lane_base;
       const int row = fb * BM + r;  // feature row within the expert
       float s0w = 1.0f, s1w = 1.0f;
       if constexpr (BITS == 8) {
@@ -433,7 +519,9 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
           if (n < ntok) {
             const size_t oidx = static_cast<size_t>(s_begin + n) * a.N + col;
             if constexpr (GATEUP) {
-              a.hout[oidx] = __float2half_rn(silu_f32(d0[i] * s0w) * (d1[i] * s1w));
+              const float gv = d0[i] * s0w;  // SiLU with the fast exponential and division: the
+              // result is rounded to fp16 (11 bits), far coarser than their error
+              a.hout[oidx] = __float2half_rn(__fdividef(gv, 1.0f + __expf(-gv)) * (d1[i] * s1w));
             } else {
               a.yout[oidx] = d0[i] * s0w;
             }
@@ -451,6 +539,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
 #ifdef MOE_GEMM_TRACE
   if (tid == 0) {
     GG_STAMP(6);
+    GG_SUM(14, gg_clock() - cta_clock0);
     unsigned smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     if (blockIdx.x < kTraceCtas)
