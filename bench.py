@@ -514,8 +514,9 @@ def main():
     # distinct routed experts it reads) / its CUDA-event duration
     per_launch = statistics.mean(d * ((gu_bytes + dn_bytes) if fused else gu_bytes) for d in distinct)
     achieved = per_launch / (k_ms / 1e3) / 1e9
-    kname = "moe_decode_fused_kernel<4>" if fused else "expert_matvec_kernel<4,32,gate/up>"
-    traffic = read_traffic("decode_fused" if fused else "gateup", args.batch)
+    kname = ("moe_decode_t1_kernel" if args.batch == 1 else "moe_decode_fused_kernel<4>") if fused \
+        else "expert_matvec_kernel<4,32,gate/up>"
+    traffic = read_traffic(("decode_t1" if args.batch == 1 else "decode_fused") if fused else "gateup", args.batch)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,

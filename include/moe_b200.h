@@ -195,8 +195,10 @@ enum moe_kernel_class {
 
 /* Handle options for moe_set_option. */
 enum moe_option {
-  /* 1 (default): batches small enough run as one cooperative launch;
-   * 0: always use the multi-kernel path. */
+  /* 1 (default): batches small enough run as one cooperative launch (a
+   * single-token kernel for T == 1 with W4 weights, else the multi-token
+   * kernel); 2: the multi-token kernel also for T == 1; 0: always use the
+   * multi-kernel path. */
   MOE_OPT_DECODE_FUSED = 1,
   /* 1: the single-launch decode kernel records per-CTA phase timestamps
    * (allocates num_SMs * 8 * 8 bytes); read them with moe_read_trace. */

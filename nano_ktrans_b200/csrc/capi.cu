@@ -40,7 +40,7 @@ struct Handle {
   int64_t* ids_tmp = nullptr;
   uint16_t* w_tmp = nullptr;
   unsigned long long* grid_bar = nullptr;  // grid-barrier arrival counter of the fused decode kernel
-  bool decode_fused = true;
+  int decode_fused = 1;  // 0 off, 1 single-token kernel for T == 1 else multi-token, 2 multi-token only
   unsigned long long* trace = nullptr;  // [num_sms][16] phase timestamps when tracing
   // prefill GEMM path: tensor maps over the activation buffers and the codes
   int32_t* tile_off = nullptr;  // [E+1]
@@ -331,6 +331,40 @@ static bool try_decode_fused(Handle* h, const uint16_t* x, const uint16_t* logit
   const moe_layer_desc& d = h->d;
   if (!h->decode_fused || (add_shared && d.shared_inter > 0)) return false;
   const int H = d.hidden_size, I = d.inter_size;
+  if (T == 1 && h->decode_fused == 1) {
+    moe::DecodeT1Params q{};
+    q.gate = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H);
+    q.up = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H);
+    q.down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
+    q.x = x;
+    q.logits = logits;
+    q.ids_in = logits ? nullptr : ids;
+    q.w_in = logits ? nullptr : wts;
+    q.mask = mask;
+    q.ids_out = ids_out;
+    q.w_out = w_out;
+    q.bits = d.bits;
+    q.E = d.num_experts;
+    q.top_k = d.top_k;
+    q.use_softmax = d.router_use_softmax;
+    q.renorm = d.normalize_topk_prob;
+    q.hbuf = h->hbuf;
+    q.out = out;
+    q.bar = h->grid_bar;
+    q.trace = h->trace;
+    q.status = h->rt.status;
+    q.num_sms = h->num_sms;
+    if (moe::decode_t1_eligible(q)) {
+      prof_mark(h, MOE_K_DECODE_FUSED, false, st);
+      const int rc = moe::launch_decode_t1(q, st);
+      prof_mark(h, MOE_K_DECODE_FUSED, true, st);
+      if (rc > 0) {
+        h->last_launches = 1;
+        return true;
+      }
+      cudaGetLastError();  // a refused launch configuration is not sticky; fall through
+    }
+  }
   moe::DecodeFusedParams p{};
   p.gate = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H);
   p.up = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H);
@@ -645,7 +679,10 @@ int moe_set_option(void* handle, int32_t option, int32_t value) {
   Handle* h = static_cast<Handle*>(handle);
   if (h == nullptr) return MOE_EINVAL;
   switch (option) {
-    case MOE_OPT_DECODE_FUSED: h->decode_fused = value != 0; return MOE_OK;
+    case MOE_OPT_DECODE_FUSED:
+      if (value < 0 || value > 2) return fail(h, MOE_EINVAL, "moe_set_option(decode fused): value must be 0, 1 or 2");
+      h->decode_fused = value;
+      return MOE_OK;
     case MOE_OPT_GEMM:
       if (value < 0 || value > 2) return fail(h, MOE_EINVAL, "moe_set_option(gemm): value must be 0, 1 or 2");
       if (value == 2 && h->has_weights && !h->gemm_maps)

@@ -76,6 +76,28 @@ bool decode_fused_eligible(int bits, int T, int E, int top_k, const QuantProj& g
 // 1 = launched; negative = not launched (caller uses the multi-kernel path).
 int launch_decode_fused(int bits, const DecodeFusedParams& p, cudaStream_t st);
 
+// Single-launch decode step for one token (decode_t1.cu).
+struct DecodeT1Params {
+  const uint16_t* x;
+  const uint16_t* logits;  // routing computed in-kernel when ids_in == nullptr
+  const int64_t* ids_in;
+  const uint16_t* w_in;
+  const uint8_t* mask;
+  int64_t* ids_out;
+  uint16_t* w_out;
+  QuantProj gate, up, down;
+  int bits, E, top_k, use_softmax, renorm;
+  float* hbuf;                // [top_k][I]
+  uint16_t* out;
+  unsigned long long* bar;    // grid-barrier arrival counter, zero-initialised, never reset
+  unsigned long long* trace;  // optional [num_sms][16] phase timestamps (ns)
+  int* status;
+  int num_sms;
+};
+bool decode_t1_eligible(const DecodeT1Params& p);
+// 1 = launched; negative = not launched.
+int launch_decode_t1(const DecodeT1Params& p, cudaStream_t st);
+
 void launch_dequant_rows(int bits, const QuantProj& p, int expert, int row0, int nrows, float* out,
                          cudaStream_t st);
 

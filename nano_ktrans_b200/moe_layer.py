@@ -146,10 +146,11 @@ class MoeLayer:
                    "moe_read_status")
         return int(st.value)
 
-    def set_decode_fused(self, enabled: bool) -> None:
-        """Run small batches as one cooperative launch (default) or always as the multi-kernel chain."""
-        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_DECODE_FUSED, int(bool(enabled))), self._h,
-                   "moe_set_option")
+    def set_decode_fused(self, mode) -> None:
+        """Small batches as one cooperative launch: True/1 (default; the single-token
+        kernel for T == 1 where it applies), 2 (the multi-token kernel also for T == 1),
+        False/0 (always the multi-kernel chain)."""
+        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_DECODE_FUSED, int(mode)), self._h, "moe_set_option")
 
     def set_gemm(self, mode: int) -> None:
         """Expert projections of the multi-kernel path: 0 matvec only, 1 tensor-core

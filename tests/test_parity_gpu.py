@@ -58,7 +58,7 @@ def test_route_matches_reference(name, cuda_device):
             assert ref == mine, (t, ref, mine)
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+@pytest.mark.parametrize("fused", [1, 2, 0], ids=["fused", "fused_multi", "chain"])
 @pytest.mark.parametrize("name", sorted(CASES))
 def test_experts_match_reference(name, fused, cuda_device):
     g, c, _, layer = _golden_layer(name, cuda_device)
@@ -200,7 +200,7 @@ def _full_case(cfg, tokens, bits, group, seed, cuda_device, zipf=None, sample_to
                 check=check_tok, shared=shared, gate_vec=gate_vec)
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+@pytest.mark.parametrize("fused", [1, 2, 0], ids=["fused", "fused_multi", "chain"])
 @pytest.mark.parametrize("tokens", [1, 3, 8, 32, 64])
 def test_qwen3_w4_decode_sweep(tokens, fused, cuda_device):
     """Config 2: Qwen3-30B-A3B-shaped W4 g128 decode at batch 1/8/32/64 (and 3),
@@ -221,7 +221,7 @@ def test_qwen3_w4_decode_sweep(tokens, fused, cuda_device):
     assert layer.read_status() == 0
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+@pytest.mark.parametrize("fused", [1, 2, 0], ids=["fused", "fused_multi", "chain"])
 def test_qwen3_w8_per_channel_decode(fused, cuda_device):
     """Config 1: W8 symmetric per-output-channel, batch 1."""
     d = _full_case(hp.QWEN3, 1, 8, 0, 7, cuda_device)
@@ -279,7 +279,7 @@ def test_mask_split_sums_to_whole(tokens, cuda_device):
     assert (whole - part).abs().max().item() <= 2 * whole.abs().max().item() * 2 ** -8
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+@pytest.mark.parametrize("fused", [1, 2, 0], ids=["fused", "fused_multi", "chain"])
 def test_empty_and_bad_inputs(fused, cuda_device):
     d = _full_case(hp.QWEN3, 4, 4, 128, 8, cuda_device)
     layer = d["layer"]
@@ -335,4 +335,54 @@ def test_fused_decode_is_one_launch_and_matches_chain(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(ids_f, ids_c) and torch.equal(w_f, w_c)
     assert torch.equal(fused, chain)
+    assert layer.read_status() == 0
+
+
+@pytest.mark.parametrize("mode", [1, 2], ids=["single_token", "multi_token"])
+def test_single_token_decode_is_one_launch_and_matches_chain(mode, cuda_device):
+    """One token: both single-launch kernels route bit-identically to the
+    multi-kernel chain and match its output (same per-row arithmetic class,
+    same combine order), and the oracle within the parity bar."""
+    d = _full_case(hp.QWEN3, 1, 4, 128, 77, cuda_device)
+    layer = d["layer"]
+    x = hp.bf16_tensor(d["x"], cuda_device)
+    lg = hp.bf16_tensor(d["logits"], cuda_device)
+    ids_f = torch.empty(1, 8, dtype=torch.int64, device=cuda_device)
+    w_f = torch.empty(1, 8, dtype=torch.bfloat16, device=cuda_device)
+    layer.set_decode_fused(mode)
+    fused = layer.forward(x, lg, out_ids=ids_f, out_weights=w_f).clone()
+    assert layer.last_launch_count() == 1
+    layer.set_decode_fused(0)
+    ids_c = torch.empty_like(ids_f)
+    w_c = torch.empty_like(w_f)
+    chain = layer.forward(x, lg, out_ids=ids_c, out_weights=w_c)
+    torch.cuda.synchronize()
+    assert torch.equal(ids_f, ids_c) and torch.equal(w_f, w_c)
+    hp.assert_paths_agree(hp.bf16_bits(fused), hp.bf16_bits(chain), MAX_ABS, MEAN_REL)
+    ref = mo.offload_forward_f32(d["x"], ids_f.cpu().numpy(), hp.bf16_bits(w_f), d["experts"])
+    hp.assert_parity(hp.bf16_bits(fused), ref, MAX_ABS, MEAN_REL)
+    assert layer.read_status() == 0
+
+
+def test_single_token_decode_repeated_and_masked(cuda_device):
+    """The single-token kernel on consecutive calls (the grid-barrier counter
+    carries over) and with an offload mask, through moe_experts_forward."""
+    d = _full_case(hp.QWEN3, 1, 4, 128, 78, cuda_device)
+    layer = d["layer"]
+    x = hp.bf16_tensor(d["x"], cuda_device)
+    ids = torch.from_numpy(d["ids"]).to(cuda_device)
+    w = hp.bf16_tensor(d["w"], cuda_device)
+    first = layer.experts_forward(x, ids, w).clone()
+    assert layer.last_launch_count() == 1
+    for _ in range(5):
+        again = layer.experts_forward(x, ids, w)
+    torch.cuda.synchronize()
+    assert torch.equal(first, again)
+    mask = np.ones(hp.QWEN3["experts"], dtype=np.uint8)
+    mask[d["ids"][0, ::2]] = 0
+    part = layer.experts_forward(x, ids, w, offload_mask=torch.from_numpy(mask).to(cuda_device))
+    torch.cuda.synchronize()
+    assert layer.last_launch_count() == 1
+    ref = mo.offload_forward_f32(d["x"], d["ids"], d["w"], d["experts"], mask.astype(bool))
+    hp.assert_parity(hp.bf16_bits(part), ref, MAX_ABS, MEAN_REL)
     assert layer.read_status() == 0
