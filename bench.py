@@ -198,7 +198,11 @@ def expert_proj_bytes(lw):
 
 def run_device(layers, x, logits, outs, steps, warmup, profile_layer_class=None):
     """Warm up eagerly, capture the L-step cycle in a CUDA graph, replay it to
-    cover `steps` steps.  Returns (ms, per-kernel avg ms or None, launches/step)."""
+    cover `steps` steps; the timed graphs hold only the layers' own kernels.
+    With profile_layer_class, a second graph of the same cycle brackets that
+    kernel class with CUDA-event record nodes and is replayed after the timed
+    region to measure the kernel alone.  Returns (ms, per-kernel avg ms or
+    None, launches/step)."""
     import torch
 
     L = len(layers)
@@ -207,21 +211,18 @@ def run_device(layers, x, logits, outs, steps, warmup, profile_layer_class=None)
     torch.cuda.synchronize()
     launches = layers[0].last_launch_count()
     full, rem = divmod(steps, L)
-    if profile_layer_class is not None:
-        for lay in layers:
-            lay.profile_begin(profile_layer_class, 1)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
-    g_full = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_full, stream=s):
-        for i in range(L):
-            layers[i].forward(x[i], logits[i], out=outs[i])
-    g_rem = None
-    if rem:
-        g_rem = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_rem, stream=s):
-            for i in range(rem):
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
                 layers[i].forward(x[i], logits[i], out=outs[i])
+        return g
+
+    g_full = capture(L)
+    g_rem = capture(rem) if rem else None
     g_full.replay()  # one untimed replay
     torch.cuda.synchronize()
     if torch.distributed.is_initialized():
@@ -241,12 +242,19 @@ def run_device(layers, x, logits, outs, steps, warmup, profile_layer_class=None)
     ms = e0.elapsed_time(e1)
     kern = None
     if profile_layer_class is not None:
+        for lay in layers:
+            lay.profile_begin(profile_layer_class, 1)
+        g_prof = capture(L)
+        g_prof.replay()  # warm
+        g_prof.replay()  # the event nodes now hold this replay's times
+        torch.cuda.synchronize()
         tot, n = 0.0, 0
         for lay in layers:
             a, b = lay.profile_end()
             tot += a
             n += b
         kern = tot / max(n, 1)
+        del g_prof
     del g_full, g_rem
     return ms, kern, launches
 
