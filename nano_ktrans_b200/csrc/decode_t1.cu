@@ -59,7 +59,7 @@ struct Args {
   unsigned long long* trace;  // [G][16] %globaltimer stamps, or null
   int* status;
   // dynamic shared-memory carve-up (byte offsets)
-  int off_lg, off_x, off_xq, off_corr, off_b, off_c, off_act, off_ys, off_tab, off_bar;
+  int off_lg, off_x, off_xq, off_corr, off_b, off_c, off_sb, off_sc, off_act, off_ys, off_tab, off_bar;
 };
 
 struct Chunk {
@@ -74,7 +74,7 @@ struct Tab {
   int act_e[kMaxK];    // routed experts, ascending
   float act_w[kMaxK];  // their routing weights
   Chunk ch[kMaxChunks];
-  int n_act, n_chunks, n_rows, abort;
+  int n_act, n_chunks, n_rows, r0, abort;
 };
 
 #define T1_TRACE(i)                                                                                 \
@@ -98,6 +98,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
   float* corr = reinterpret_cast<float*>(smem + a.off_corr);
   unsigned char* reg_b = smem + a.off_b;
   unsigned char* reg_c = smem + a.off_c;
+  uint16_t* sc_b = reinterpret_cast<uint16_t*>(smem + a.off_sb);  // [row][gate, up][gate.sstride] scales
+  uint16_t* sc_c = reinterpret_cast<uint16_t*>(smem + a.off_sc);  // [expert][row][down.sstride] scales
   float4* act4 = reinterpret_cast<float4*>(smem + a.off_act);
   float* ys = reinterpret_cast<float*>(smem + a.off_ys);  // [k][kRowsC]
   Tab& tb = *reinterpret_cast<Tab*>(smem + a.off_tab);
@@ -156,28 +158,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
       tb.act_w[rank] = w;
     }
     const int n_act = __popc(__ballot_sync(kFullMask, valid));
+    // this CTA's share [r0, r1) of the flat (expert, row) space, cut at multiples
+    // of kChunkRows (I is a multiple of it, so no chunk spans two experts):
+    // lane j builds chunk j
+    const int total = n_act * I;
+    const int r0 = static_cast<int>((static_cast<long long>(total) * cta) / G);
+    const int r1 = static_cast<int>((static_cast<long long>(total) * (cta + 1)) / G);
+    const int c0 = r0 / kChunkRows;
+    const int nc = r1 > r0 ? (r1 + kChunkRows - 1) / kChunkRows - c0 : 0;
+    const int rowpair = H;  // gate + up codes of one row: 2 x H/2 bytes
+    for (int j = lane; j < nc && j < kMaxChunks; j += 32) {
+      const int b = max(r0, (c0 + j) * kChunkRows), e = min(r1, (c0 + j + 1) * kChunkRows);
+      const int ai = b / I;
+      tb.ch[j] = Chunk{ai, b - ai * I, e - b, b - r0, (b - r0) * rowpair};
+    }
     if (lane == 0) {
       tb.n_act = n_act;
-      // this CTA's share of the flat (expert, row) space, cut into chunks
-      const int total = n_act * I;
-      const int r0 = static_cast<int>((static_cast<long long>(total) * cta) / G);
-      const int r1 = static_cast<int>((static_cast<long long>(total) * (cta + 1)) / G);
-      const int rowpair = 2 * (H / 2 + a.gate.sstride * 2);
-      int nc = 0, r = r0, ai = total > 0 ? r0 / I : 0, row = total > 0 ? r0 - ai * I : 0;
-      while (r < r1 && nc < kMaxChunks) {
-        const int n = min(kChunkRows, min(I - row, r1 - r));
-        tb.ch[nc] = Chunk{ai, row, n, r - r0, (r - r0) * rowpair};
-        ++nc;
-        r += n;
-        row += n;
-        if (row == I) {
-          row = 0;
-          ++ai;
-        }
-      }
-      if (r < r1) fail();  // chunk table overflow: cannot happen within the launch limits
-      tb.n_chunks = nc;
+      tb.n_chunks = min(nc, kMaxChunks);
       tb.n_rows = r1 - r0;
+      tb.r0 = r0;
+      if (nc > kMaxChunks) fail();  // chunk table overflow: excluded by the launch limits
     }
   } else if (in_ok) {
     // bf16 operand words + one correction per 32-code chunk (w4_pack_x)
@@ -201,41 +201,65 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
 
   // ---- 2. request every byte this CTA will read -----------------------------------------
   const int n_act = tb.n_act, nchunks = tb.n_chunks;
-  const size_t rb_b = static_cast<size_t>(H) / 2, sb_b = static_cast<size_t>(a.gate.sstride) * 2;
-  const size_t rb_c = static_cast<size_t>(I) / 2, sb_c = static_cast<size_t>(a.down.sstride) * 2;
+  const size_t rb_b = static_cast<size_t>(H) / 2, rb_c = static_cast<size_t>(I) / 2;
+  const int ssb = a.gate.sstride, ssc = a.down.sstride;  // bf16 per scale row (multiples of 8)
   const int n0 = (cta * H) / G;
   const int nrc = ((cta + 1) * H) / G - n0;
-  const size_t per_c = static_cast<size_t>(nrc) * (rb_c + sb_c);
+  const size_t per_c = static_cast<size_t>(nrc) * rb_c;
+  const int nrows = tb.n_rows, r0 = tb.r0;
   const bool issued = !*abort_flag;  // CTA-uniform: nothing writes the flag between the barrier above and here
-  if (issued) {
-    if (tid < nchunks) {
-      const Chunk c = tb.ch[tid];
-      const uint32_t bar = ac::smem_u32(&bars[2 + tid]);
+  if (issued && warp == 0) {
+    // bulk copies of the codes only (the TMA unit takes one request at a time,
+    // so chunk 0 goes first, then the other gate/up chunks, then the down blocks)
+    auto issue_chunk = [&](int j) {
+      const Chunk c = tb.ch[j];
+      const uint32_t bar = ac::smem_u32(&bars[2 + j]);
       const uint32_t dst = ac::smem_u32(reg_b + c.off);
       const size_t rix = static_cast<size_t>(tb.act_e[c.a]) * I + c.row0;
-      const uint32_t cb = static_cast<uint32_t>(c.n * rb_b), sbt = static_cast<uint32_t>(c.n * sb_b);
-      ac::mbar_arrive_expect_tx(bar, 2 * cb + 2 * sbt);
+      const uint32_t cb = static_cast<uint32_t>(c.n * rb_b);
+      ac::mbar_arrive_expect_tx(bar, 2 * cb);
       ac::bulk_g2s(dst, a.gate.q + rix * rb_b, cb, bar);
       ac::bulk_g2s(dst + cb, a.up.q + rix * rb_b, cb, bar);
-      ac::bulk_g2s(dst + 2 * cb, a.gate.s + rix * a.gate.sstride, sbt, bar);
-      ac::bulk_g2s(dst + 2 * cb + sbt, a.up.s + rix * a.up.sstride, sbt, bar);
-    } else if (warp == kWarps - 1 && nrc > 0 && n_act > 0) {
+    };
+    if (lane == 0 && nchunks > 0) issue_chunk(0);
+    __syncwarp();
+    for (int j = 1 + lane; j < nchunks; j += 32) issue_chunk(j);
+    __syncwarp();
+    if (nrc > 0 && n_act > 0) {
       const uint32_t bar = ac::smem_u32(&bars[1]);
       if (lane == 0) ac::mbar_arrive_expect_tx(bar, static_cast<uint32_t>(n_act * per_c));
       __syncwarp();
       for (int i = lane; i < n_act; i += 32) {
         const size_t rix = static_cast<size_t>(tb.act_e[i]) * H + n0;
-        const uint32_t o = ac::smem_u32(reg_c + i * per_c);
-        ac::bulk_g2s(o, a.down.q + rix * rb_c, static_cast<uint32_t>(nrc * rb_c), bar);
-        ac::bulk_g2s(o + static_cast<uint32_t>(nrc * rb_c), a.down.s + rix * a.down.sstride,
-                     static_cast<uint32_t>(nrc * sb_c), bar);
+        ac::bulk_g2s(ac::smem_u32(reg_c + i * per_c), a.down.q + rix * rb_c, static_cast<uint32_t>(per_c), bar);
       }
     }
+  } else if (issued) {
+    // the other warps fetch the scale rows with plain 16-byte loads meanwhile
+    const int vb = ssb / 8, vc = ssc / 8;  // 16-byte vectors per scale row
+    const int nb = nrows * 2 * vb, ncv = n_act * nrc * vc;
+    for (int v = tid - 32; v < nb + ncv; v += kThreads - 32) {
+      const uint4* src;
+      uint4* dst;
+      if (v < nb) {
+        const int lr = v / (2 * vb), rem = v - lr * 2 * vb, pj = rem / vb, q = rem - pj * vb;
+        const int gr = r0 + lr, ai = gr / I;
+        const size_t srow = static_cast<size_t>(tb.act_e[ai]) * I + (gr - ai * I);
+        src = reinterpret_cast<const uint4*>((pj == 0 ? a.gate.s : a.up.s) + srow * ssb) + q;
+        dst = reinterpret_cast<uint4*>(sc_b + (lr * 2 + pj) * ssb) + q;
+      } else {
+        const int u = v - nb, ir = u / vc, q = u - ir * vc;
+        const int i = ir / nrc, rs = ir - i * nrc;
+        src = reinterpret_cast<const uint4*>(a.down.s + (static_cast<size_t>(tb.act_e[i]) * H + n0 + rs) * ssc) + q;
+        dst = reinterpret_cast<uint4*>(sc_c + ir * ssc) + q;
+      }
+      *dst = __ldg(src);
+    }
   }
+  __syncthreads();  // scales in shared memory; the code copies are still in flight
   T1_TRACE(2);
 
   // ---- 3. gate/up rows as their chunks land -----------------------------------------------
-  const int nrows = tb.n_rows;
   for (int lr = warp; lr < nrows; lr += kWarps) {
     if (__any_sync(kFullMask, *abort_flag)) break;
     int ci = 0;
@@ -249,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
     const unsigned char* base = reg_b + c.off;
     const unsigned char* wg = base + rr * rb_b;
     const unsigned char* wu = base + c.n * rb_b + rr * rb_b;
-    const uint16_t* sg = reinterpret_cast<const uint16_t*>(base + 2 * c.n * rb_b + rr * sb_b);
-    const uint16_t* su = reinterpret_cast<const uint16_t*>(base + 2 * c.n * rb_b + c.n * sb_b + rr * sb_b);
+    const uint16_t* sg = sc_b + (lr * 2) * ssb;
+    const uint16_t* su = sc_b + (lr * 2 + 1) * ssb;
     const int gsh = 31 - __clz(a.gate.group / kCodes);  // chunks per scale group, a power of two
     float ag = 0.0f, au = 0.0f;
 #pragma unroll 2
@@ -310,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
       const bool live = item < items;
       const int i = live ? item / nrc : 0, rs = live ? item - i * nrc : 0;
       const unsigned char* wd = reg_c + i * per_c + static_cast<size_t>(rs) * rb_c;
-      const uint16_t* sd = reinterpret_cast<const uint16_t*>(reg_c + i * per_c + nrc * rb_c + rs * sb_c);
+      const uint16_t* sd = sc_c + (i * nrc + rs) * ssc;
       float ay = 0.0f;
       if (live) {
 #pragma unroll 3
@@ -360,10 +384,10 @@ struct T1Plan {
 static T1Plan t1_plan(const DecodeT1Params& p) {
   T1Plan pl;
   const int H = p.gate.k, I = p.gate.n, k = p.top_k, G = p.num_sms;
-  const size_t rowpair = 2 * (static_cast<size_t>(H) / 2 + p.gate.sstride * 2);
+  const size_t rowpair = static_cast<size_t>(H);  // gate + up codes of one row
   const size_t rows_b = (static_cast<size_t>(k) * I + G - 1) / G;
   const int nrc = (H + G - 1) / G;
-  const size_t per_c = static_cast<size_t>(nrc) * (static_cast<size_t>(I) / 2 + p.down.sstride * 2);
+  const size_t per_c = static_cast<size_t>(nrc) * (static_cast<size_t>(I) / 2);
   const int it_b = (H / 32 + 31) / 32, it_c = (I / 32 + 7) / 8;
   size_t off = 0;
   auto take = [&](size_t bytes, size_t align) {
@@ -374,6 +398,8 @@ static T1Plan t1_plan(const DecodeT1Params& p) {
   };
   pl.a.off_b = take(rows_b * rowpair, 128);
   pl.a.off_c = take(static_cast<size_t>(k) * per_c, 128);
+  pl.a.off_sb = take(rows_b * 2 * p.gate.sstride * 2, 16);
+  pl.a.off_sc = take(static_cast<size_t>(k) * nrc * p.down.sstride * 2, 16);
   pl.a.off_x = take(static_cast<size_t>(H) * 2, 128);
   pl.a.off_lg = take(static_cast<size_t>(p.E) * 2, 128);
   pl.a.off_xq = take(static_cast<size_t>(it_b) * 32 * 4 * 16, 16);
@@ -383,7 +409,7 @@ static T1Plan t1_plan(const DecodeT1Params& p) {
   pl.a.off_tab = take(sizeof(t1::Tab), 16);
   pl.a.off_bar = take(8 * (2 + t1::kMaxChunks), 8);
   pl.smem = off;
-  const size_t chunks = (rows_b + t1::kChunkRows - 1) / t1::kChunkRows + k + 1;
+  const size_t chunks = (rows_b + t1::kChunkRows - 1) / t1::kChunkRows + 1;  // aligned chunks over the share
   if (off > 227 * 1024 || nrc > t1::kRowsC || chunks > static_cast<size_t>(t1::kMaxChunks)) pl.smem = 0;
   return pl;
 }

@@ -80,21 +80,26 @@ MOE_DEV void route_token_warp(const uint16_t* __restrict__ row, int E, int top_k
     key[i] = e < E ? rank_key(v[i], e) : 0u;  // valid keys are never 0
   }
 
+  // each lane's keys in descending order (compare-exchange passes on registers)
+#pragma unroll
+  for (int p = 0; p < EPL - 1; ++p) {
+#pragma unroll
+    for (int i = 0; i < EPL - 1 - p; ++i) {
+      const uint32_t hi = max(key[i], key[i + 1]), lo = min(key[i], key[i + 1]);
+      key[i] = hi;
+      key[i + 1] = lo;
+    }
+  }
   float my_val = 0.0f, sum = 0.0f, v0 = 0.0f, exsum = 0.0f;
   my_id = 0;
 #pragma unroll 1
   for (int j = 0; j < top_k; ++j) {
-    uint32_t best = 0;
-    int bi = 0;
+    const uint32_t m = __reduce_max_sync(kFullMask, key[0]);
+    if (key[0] == m) {  // keys are unique: exactly one lane owns the pick and drops it
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      if (key[i] > best) {
-        best = key[i];
-        bi = i;
-      }
+      for (int i = 0; i < EPL - 1; ++i) key[i] = key[i + 1];
+      key[EPL - 1] = 0;
     }
-    const uint32_t m = __reduce_max_sync(kFullMask, best);
-    if (best == m) key[bi] = 0;  // keys are unique: exactly one lane owns the pick
     const float val = rank_key_value(m);
     if (lane == j) {
       my_val = val;
@@ -102,7 +107,7 @@ MOE_DEV void route_token_warp(const uint16_t* __restrict__ row, int E, int top_k
     }
     sum += val;  // slot-order fp32 sum (a bf16 sum accumulates in fp32)
     if (j == 0) v0 = val;
-    exsum += expf(val - v0);
+    if (!use_softmax) exsum += expf(val - v0);  // Mixtral: softmax over the picks
   }
 
   float w = my_val;
