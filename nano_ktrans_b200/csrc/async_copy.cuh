@@ -59,11 +59,12 @@ MOE_DEV unsigned long long global_ns() {
 // Grid-wide barrier for a cooperative launch.  The 64-bit arrival counter
 // only grows: a CTA's arrival returns n, its launch's barrier is complete
 // when the counter reaches (n / G + 1) * G.  No reset, no second atomic.
-// Returns false if the wait hit its iteration limit.
+// Returns false if the wait hit its iteration limit.  Only thread 0 fences and
+// polls: the block barrier on either side orders the other threads' accesses.
 MOE_DEV bool grid_sync_bounded(unsigned long long* bar, int* ok_smem) {
-  __threadfence();
-  __syncthreads();
+  __syncthreads();  // the CTA's writes are ordered before thread 0's fence (cumulativity)
   if (threadIdx.x == 0) {
+    __threadfence();
     cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> count(*bar);
     const unsigned long long g = gridDim.x;
     const unsigned long long target = (count.fetch_add(1ull, cuda::memory_order_acq_rel) / g + 1) * g;
