@@ -7,6 +7,8 @@ Public API (mirrors the reference's names):
 * ``CudaMoEBackend`` — the ``"cuda"`` expert backend
 * ``HybridMoE`` — the MoE layer using it
 * ``MoeLayer`` — direct access to the C-ABI handle (route / experts / fused forward)
+* ``EpMoeLayer``, ``plan_placement``, ``shard_layer``, ``TorchDistComm`` — expert
+  parallelism over the ranks of a process group
 """
 from .offload_backend import ExpertOffloadBackend, normalize_offload_backend_name
 from .weights import GPTQLinearWeight, LayerWeights, quantize_symmetric, stack_layer
@@ -14,6 +16,7 @@ from .weights import GPTQLinearWeight, LayerWeights, quantize_symmetric, stack_l
 __all__ = [
     "ExpertOffloadBackend", "normalize_offload_backend_name", "GPTQLinearWeight", "LayerWeights",
     "quantize_symmetric", "stack_layer", "CudaMoEBackend", "HybridMoE", "MoeLayer",
+    "EpMoeLayer", "plan_placement", "shard_layer", "TorchDistComm",
 ]
 
 
@@ -27,4 +30,7 @@ def __getattr__(name):
     if name == "MoeLayer":
         from .moe_layer import MoeLayer
         return MoeLayer
+    if name in ("EpMoeLayer", "plan_placement", "shard_layer", "TorchDistComm"):
+        from . import expert_parallel
+        return getattr(expert_parallel, name)
     raise AttributeError(name)
