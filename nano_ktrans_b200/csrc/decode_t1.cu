@@ -6,7 +6,10 @@
 // nano_ktrans/kernels/cpu_moe.py:491-539 expert loop and index_add_
 // combine, quantized_ops.py:86-124 grouped matvec arithmetic).
 //
-// One CTA of 1024 threads per SM, launched cooperatively:
+// One CTA of 1024 threads per SM, launched cooperatively and as a
+// programmatic dependent of the previous kernel on the stream (its launch
+// overlaps that kernel's tail; griddepcontrol.wait precedes every global
+// access):
 //  1. Thread 0 bulk-copies the token's logits and activations into shared
 //     memory at entry.  Warp 0 routes the token (route_warp.cuh) and orders
 //     its experts ascending; the other warps pack x into bf16 operand words.
@@ -14,15 +17,18 @@
 //     over the CTAs.  Each CTA's whole share (about 42 row pairs, 88 KB at
 //     Qwen3 shapes) is requested at once, in chunks of up to 8 rows with one
 //     mbarrier each, followed by every down-projection block the CTA will
-//     need in phase 4.  Nothing waits for shared memory to be recycled.
+//     need in phase 5.  Nothing waits for shared memory to be recycled.
 //  3. Warp w computes rows w, w+32, ... as soon as each row's chunk lands:
 //     gate and up dot products with the exact bf16-operand W4 arithmetic of
 //     common.cuh, warp-shuffle reduced, SiLU(gate)*up written to global h.
-//  4. One grid barrier; h of every routed expert is staged in shared memory.
-//  5. CTA c owns output rows [c*H/G, (c+1)*H/G): 8 lanes per (expert, row)
-//     compute the down projection from the blocks already in shared memory,
-//     then one thread per row adds w * y over the experts in ascending
-//     expert order in fp32 (the reference's index_add_ order) and writes bf16.
+//  4. One grid barrier; every CTA stages h of all routed experts in shared
+//     memory as bf16 (high, low) operand pairs.
+//  5. CTA c owns output rows [c*H/G, (c+1)*H/G): 16-row tiles of each routed
+//     expert's down block (already in shared memory) against h on the
+//     warp-level tensor-core path (mma_gemv.cuh), B's column halves carrying
+//     the high and low parts of h; then one warp per row adds w * y over the
+//     experts in ascending expert order in fp32 (the reference's index_add_
+//     order) and writes bf16.
 // Every wait is bounded; on expiry the kernel records kStatusTimeout, stops
 // computing, still arrives at the grid barrier and lets its issued copies
 // land before exiting.
@@ -31,6 +37,7 @@
 #include "async_copy.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "mma_gemv.cuh"
 #include "route_warp.cuh"
 
 namespace moe {
@@ -59,7 +66,7 @@ struct Args {
   unsigned long long* trace;  // [G][16] %globaltimer stamps, or null
   int* status;
   // dynamic shared-memory carve-up (byte offsets)
-  int off_lg, off_x, off_xq, off_corr, off_b, off_c, off_sb, off_sc, off_act, off_ys, off_tab, off_bar;
+  int off_lg, off_x, off_xq, off_corr, off_b, off_c, off_sb, off_sc, off_act, off_cc, off_tt, off_ys, off_tab, off_bar;
 };
 
 struct Chunk {
@@ -77,9 +84,12 @@ struct Tab {
   int n_act, n_chunks, n_rows, r0, abort;
 };
 
-#define T1_TRACE(i)                                                                                 \
-  do {                                                                                              \
-    if (a.trace != nullptr && threadIdx.x == 0) a.trace[blockIdx.x * 16 + (i)] = ac::global_ns(); \
+// Phase stamps (MOE_OPT_TRACE), thread 0 of each CTA: slot 0 holds %globaltimer
+// at entry (ns), slots 1-12 SM clock cycles since entry.
+#define T1_TRACE(i)                                                                      \
+  do {                                                                                   \
+    if (a.trace != nullptr && threadIdx.x == 0)                                          \
+      a.trace[blockIdx.x * 16 + (i)] = (i) == 0 ? ac::global_ns() : clock64() - t_entry; \
   } while (0)
 
 template <int EPL>
@@ -100,8 +110,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
   unsigned char* reg_c = smem + a.off_c;
   uint16_t* sc_b = reinterpret_cast<uint16_t*>(smem + a.off_sb);  // [row][gate, up][gate.sstride] scales
   uint16_t* sc_c = reinterpret_cast<uint16_t*>(smem + a.off_sc);  // [expert][row][down.sstride] scales
-  float4* act4 = reinterpret_cast<float4*>(smem + a.off_act);
-  float* ys = reinterpret_cast<float*>(smem + a.off_ys);  // [k][kRowsC]
   Tab& tb = *reinterpret_cast<Tab*>(smem + a.off_tab);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_bar);  // [0] inputs, [1] phase-5 blocks, [2+i] chunk i
   __shared__ int grid_ok;
@@ -112,6 +120,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
   };
 
   const bool route_here = a.ids_in == nullptr;
+  // Programmatic dependent launch: this grid may start while the previous
+  // kernel on the stream finishes; nothing in global memory is touched before
+  // that kernel has completed and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const long long t_entry = clock64();
   T1_TRACE(0);
   if (tid == 0) {
     for (int i = 0; i < 2 + kMaxChunks; ++i) ac::mbar_init(ac::smem_u32(&bars[i]), 1);
@@ -126,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
   __syncthreads();
   const bool in_ok = __all_sync(kFullMask, ac::mbar_wait_bounded(ac::smem_u32(&bars[0]), 0u));
   if (!in_ok && lane == 0) fail();
+  T1_TRACE(1);
 
   // ---- 1. routing (warp 0) and x packing (the other warps) --------------------------
   const int nch_b = H / kCodes, it_b = (nch_b + 31) / 32;
@@ -141,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
       }
     } else if (in_ok) {
       route_token_warp<EPL>(lg, E, k, a.use_softmax != 0, a.renorm != 0, id, w);
+      T1_TRACE(2);
       if (cta == 0 && lane < k) {
         a.ids_out[lane] = id;
         a.w_out[lane] = f32_to_bf16(w);
@@ -149,8 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
     const bool valid = lane < k && id >= 0 && (a.mask == nullptr || a.mask[id] != 0);
     // rank among the valid pairs by (expert, slot)
     int rank = 0;
+    const int vid = valid ? id : -1;
+#pragma unroll 8
     for (int m = 0; m < k; ++m) {
-      const int em = __shfl_sync(kFullMask, valid ? id : -1, m);
+      const int em = __shfl_sync(kFullMask, vid, m);
       rank += (em >= 0 && (em < id || (em == id && m < lane))) ? 1 : 0;
     }
     if (valid) {
@@ -162,8 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
     // of kChunkRows (I is a multiple of it, so no chunk spans two experts):
     // lane j builds chunk j
     const int total = n_act * I;
-    const int r0 = static_cast<int>((static_cast<long long>(total) * cta) / G);
-    const int r1 = static_cast<int>((static_cast<long long>(total) * (cta + 1)) / G);
+    const int r0 = static_cast<int>(static_cast<uint32_t>(total) * cta / static_cast<uint32_t>(G));
+    const int r1 = static_cast<int>(static_cast<uint32_t>(total) * (cta + 1) / static_cast<uint32_t>(G));
     const int c0 = r0 / kChunkRows;
     const int nc = r1 > r0 ? (r1 + kChunkRows - 1) / kChunkRows - c0 : 0;
     const int rowpair = H;  // gate + up codes of one row: 2 x H/2 bytes
@@ -179,6 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
       tb.r0 = r0;
       if (nc > kMaxChunks) fail();  // chunk table overflow: excluded by the launch limits
     }
+    T1_TRACE(3);
   } else if (in_ok) {
     // bf16 operand words + one correction per 32-code chunk (w4_pack_x)
     const int H8 = H / 8;
@@ -197,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
     }
   }
   __syncthreads();
-  T1_TRACE(1);
+  T1_TRACE(4);
 
   // ---- 2. request every byte this CTA will read -----------------------------------------
   const int n_act = tb.n_act, nchunks = tb.n_chunks;
@@ -255,15 +274,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
       }
       *dst = __ldg(src);
     }
+    // phase-5 task table: (expert slot, 16-row tile, 128-code group, scale index)
+    const int ts = (nrc + 15) / 16, ngc = I / 128, gpg = a.down.group / 128;
+    int2* ttab = reinterpret_cast<int2*>(smem + a.off_tt);
+    for (int t = tid - 32; t < n_act * ts * ngc; t += kThreads - 32) {
+      const int G = t % ngc, tile = t / ngc, i = tile / ts, m = tile - i * ts;
+      ttab[t] = make_int2((i << 8) | m, G | ((G / gpg) << 16));
+    }
   }
   __syncthreads();  // scales in shared memory; the code copies are still in flight
-  T1_TRACE(2);
+  T1_TRACE(5);
 
   // ---- 3. gate/up rows as their chunks land -----------------------------------------------
   for (int lr = warp; lr < nrows; lr += kWarps) {
     if (__any_sync(kFullMask, *abort_flag)) break;
-    int ci = 0;
-    while (ci + 1 < nchunks && tb.ch[ci + 1].lr0 <= lr) ++ci;
+    const int ci = (tb.r0 + lr) / kChunkRows - tb.r0 / kChunkRows;
     const Chunk c = tb.ch[ci];
     if (!__all_sync(kFullMask, ac::mbar_wait_bounded(ac::smem_u32(&bars[2 + ci]), 0u))) {
       if (lane == 0) fail();
@@ -298,73 +323,118 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
     }
     if (lane == 0) a.hbuf[static_cast<size_t>(c.a) * I + c.row0 + rr] = silu_f32(ag) * au;
   }
-  T1_TRACE(3);
+  T1_TRACE(6);  // (stamp 7 marks the same point: h is written by the rows themselves)
+  T1_TRACE(7);
 
   // ---- 4. grid barrier, stage h ----------------------------------------------------------------
   const bool passed = ac::grid_sync_bounded(a.bar, &grid_ok);
   if (!passed && tid == 0) fail();
-  T1_TRACE(4);
-  const int nch_c = I / kCodes, it_c = (nch_c + 7) / 8, k4p_c = it_c * 8 * kQ;
-  const int I4 = I / 4;
-  for (int idx = tid; idx < n_act * I4; idx += kThreads) {
-    const int s = idx / I4, f = idx - s * I4;
-    const int c = f / kQ, q = f - c * kQ;
-    float4 v = __ldcg(reinterpret_cast<const float4*>(a.hbuf + static_cast<size_t>(s) * I) + f);
-    v.x *= act_prescale<4>(4 * f);
-    v.y *= act_prescale<4>(4 * f + 1);
-    v.z *= act_prescale<4>(4 * f + 2);
-    v.w *= act_prescale<4>(4 * f + 3);
-    act4[s * k4p_c + ((c >> 3) * kQ + q) * 8 + (c & 7)] = v;
-  }
-  __syncthreads();
-  T1_TRACE(5);
-
-  // ---- 5. down rows + ordered combine ---------------------------------------------------------------
-  const bool c_ok = !issued || nrc == 0 || n_act == 0 || ac::mbar_wait_bounded(ac::smem_u32(&bars[1]), 0u);
-  if (!c_ok) fail();
-  __syncthreads();
-  T1_TRACE(6);
-  const bool ok5 = !*abort_flag;  // CTA-uniform after the barrier above
-  if (ok5) {
-    const int items = n_act * nrc;
-    const int sl8 = lane & 7;
-    const int gshc = 31 - __clz(a.down.group / kCodes);
-    for (int item0 = warp * 4; item0 < items; item0 += kWarps * 4) {
-      const int item = item0 + (lane >> 3);
-      const bool live = item < items;
-      const int i = live ? item / nrc : 0, rs = live ? item - i * nrc : 0;
-      const unsigned char* wd = reg_c + i * per_c + static_cast<size_t>(rs) * rb_c;
-      const uint16_t* sd = sc_c + (i * nrc + rs) * ssc;
-      float ay = 0.0f;
-      if (live) {
-#pragma unroll 3
-        for (int it = 0; it < it_c; ++it) {
-          const int ch = it * 8 + sl8;
-          if (ch < nch_c) {
-            const uint4 v = *reinterpret_cast<const uint4*>(wd + 16 * ch);
-            const float sc = bf16_to_f32(sd[ch >> gshc]);
-            ay = fmaf(sc, chunk_dot<4>(v, act4 + i * k4p_c + (it * kQ) * 8 + sl8, 8), ay);
-          }
-        }
-      }
+  T1_TRACE(8);
+  // Stage h as bf16 (hi, lo) operand words: word w = 4c + q (8 activations,
+  // 32-code chunk c) of expert slot s goes to hq[s * I/8 + q * I/32 + c] (high
+  // parts) and the same index past lo_off (low parts) in the w4_pack_x pair
+  // order; one correction 136 * sum(hi + lo) per 128-code group.
+  const int w8 = I / 8, w32 = I / 32, ngc = I / 128, ts = (nrc + 15) / 16;
+  const int lo_off = k * w8 + 4;  // the low plane sits 64 bytes off the high plane's bank alignment
+  uint4* hq = reinterpret_cast<uint4*>(smem + a.off_act);
+  float* corr_c = reinterpret_cast<float*>(smem + a.off_cc);  // [slot][group]
+  {
+    const float4* h4 = reinterpret_cast<const float4*>(a.hbuf);
+    const int nw = n_act * w8;
+    for (int base = 0; base < nw; base += kThreads) {
+      const int wd = base + tid;
+      const bool ok = wd < nw;
+      float cs = 0.0f;
+      if (ok) {
+        const int sl = wd / w8, wi = wd - sl * w8;
+        const int dst = sl * w8 + (wi & 3) * w32 + (wi >> 2);
+        const float4 v0 = __ldcg(h4 + 2 * wd), v1 = __ldcg(h4 + 2 * wd + 1);
+        const float hv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint16_t hi[8], lo[8];
 #pragma unroll
-      for (int o = 4; o > 0; o >>= 1) ay += __shfl_xor_sync(kFullMask, ay, o);
-      if (live && sl8 == 0) ys[i * kRowsC + rs] = ay;
+        for (int e = 0; e < 8; ++e) split_bf16(hv[e], hi[e], lo[e]);
+        hq[dst] = make_uint4(pack_bf16x2(hi[0], hi[4]), pack_bf16x2(hi[1], hi[5]), pack_bf16x2(hi[2], hi[6]),
+                             pack_bf16x2(hi[3], hi[7]));
+        hq[lo_off + dst] = make_uint4(pack_bf16x2(lo[0], lo[4]), pack_bf16x2(lo[1], lo[5]),
+                                      pack_bf16x2(lo[2], lo[6]), pack_bf16x2(lo[3], lo[7]));
+        float sv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sv[e] = bf16_to_f32(hi[e]) + bf16_to_f32(lo[e]);  // exact
+        cs = ((sv[0] + sv[1]) + (sv[2] + sv[3])) + ((sv[4] + sv[5]) + (sv[6] + sv[7]));
+      }
+      // a 128-code group is 16 consecutive words: aligned 16-lane segments
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) cs += __shfl_xor_sync(kFullMask, cs, o);
+      if (ok && (wd & 15) == 0) corr_c[wd >> 4] = 136.0f * cs;
     }
   }
   __syncthreads();
-  T1_TRACE(7);
-  if (ok5 && tid < nrc) {
-    float acc = 0.0f;
-    for (int i = 0; i < n_act; ++i) acc = __fadd_rn(acc, __fmul_rn(ys[i * kRowsC + tid], tb.act_w[i]));
-    a.out[n0 + tid] = f32_to_bf16(acc);
+  T1_TRACE(9);
+
+  // ---- 5. down tiles + ordered combine ---------------------------------------------------------------
+  const bool c_ok = !issued || nrc == 0 || n_act == 0 || ac::mbar_wait_bounded(ac::smem_u32(&bars[1]), 0u);
+  if (!c_ok) fail();
+  __syncthreads();
+  T1_TRACE(10);
+  const bool ok5 = !*abort_flag;  // CTA-uniform after the barrier above
+  // Tile = 16 of the CTA's output rows of one expert slot (rows past nrc repeat
+  // the last one).  B's columns 0-3 carry the high bf16 parts of h, columns 4-7
+  // the low parts, so lanes t and t ^ 2 hold the two halves of each row sum.
+  // Task (tile, group): one warp, 8 mma; lanes t == 0 store s * (sum - corr).
+  float* part_c = reinterpret_cast<float*>(smem + a.off_ys);  // [slot][tile][16 rows][group]
+  const int g4 = lane >> 2, t4 = lane & 3;
+  if (ok5) {
+    const int ntask = n_act * ts * ngc;
+    const int2* ttab = reinterpret_cast<const int2*>(smem + a.off_tt);
+    for (int task = warp; task < ntask; task += kWarps) {
+      const int2 te = ttab[task];
+      const int i = te.x >> 8, m = te.x & 255, G = te.y & 0xffff, si = te.y >> 16;
+      const int ch = G * 4 + t4;
+      const uint4* hp = hq + (g4 < 4 ? 0 : lo_off) + i * w8 + ch;
+      const uint4 src[4] = {hp[0], hp[w32], hp[2 * w32], hp[3 * w32]};
+      const int rl = min(m * 16 + g4, nrc - 1), rh = min(m * 16 + 8 + g4, nrc - 1);
+      const unsigned char* wb = reg_c + i * per_c + 16 * ch;
+      const uint4 wl = *reinterpret_cast<const uint4*>(wb + static_cast<size_t>(rl) * rb_c);
+      const uint4 wh = *reinterpret_cast<const uint4*>(wb + static_cast<size_t>(rh) * rb_c);
+      float d[4];
+      w4_group_mma(wl, wh, src, d);
+      const float sl = d[0] + __shfl_xor_sync(kFullMask, d[0], 2);
+      const float sh = d[2] + __shfl_xor_sync(kFullMask, d[2], 2);
+      if (t4 == 0) {
+        const float cg = corr_c[i * ngc + G];
+        float* p = part_c + (i * ts + m) * 16 * ngc + G;  // [slot][tile][row][group]
+        p[g4 * ngc] = bf16_to_f32(sc_c[(i * nrc + rl) * ssc + si]) * (sl - cg);
+        p[(8 + g4) * ngc] = bf16_to_f32(sc_c[(i * nrc + rh) * ssc + si]) * (sh - cg);
+      }
+    }
+  }
+  __syncthreads();
+  T1_TRACE(11);
+  // one warp per output row: lane i forms w_i * y_i, the products are added in
+  // slot (ascending expert) order in fp32
+  if (ok5) {
+    for (int rs = warp; rs < nrc; rs += kWarps) {
+      const int m = rs >> 4, r = rs & 15;
+      float yw = 0.0f;
+      if (lane < n_act) {
+        const float* p = part_c + ((lane * ts + m) * 16 + r) * ngc;
+        float yv = 0.0f;
+#pragma unroll 4
+        for (int G = 0; G < ngc; ++G) yv += p[G];
+        yw = __fmul_rn(yv, tb.act_w[lane]);
+      }
+      float acc = 0.0f;
+#pragma unroll 8
+      for (int i = 0; i < n_act; ++i) acc = __fadd_rn(acc, __shfl_sync(kFullMask, yw, i));
+      if (lane == 0) a.out[n0 + rs] = f32_to_bf16(acc);
+    }
   }
   // copies issued but never waited on (abort path) must land before exit
   if (issued && !ok5 && tid == 0) {
     for (int i = 0; i < nchunks; ++i) ac::mbar_wait_bounded(ac::smem_u32(&bars[2 + i]), 0u);
     if (nrc > 0 && n_act > 0) ac::mbar_wait_bounded(ac::smem_u32(&bars[1]), 0u);
   }
-  T1_TRACE(8);
+  T1_TRACE(12);
 }
 
 }  // namespace t1
@@ -404,8 +474,11 @@ static T1Plan t1_plan(const DecodeT1Params& p) {
   pl.a.off_lg = take(static_cast<size_t>(p.E) * 2, 128);
   pl.a.off_xq = take(static_cast<size_t>(it_b) * 32 * 4 * 16, 16);
   pl.a.off_corr = take(static_cast<size_t>(it_b) * 32 * 4, 16);
-  pl.a.off_act = take(static_cast<size_t>(k) * it_c * 8 * 8 * 16, 16);
-  pl.a.off_ys = take(static_cast<size_t>(k) * t1::kRowsC * 4, 16);
+  const size_t ngc = I / 128, ts = (nrc + 15) / 16;
+  pl.a.off_act = take(static_cast<size_t>(k) * I * 4 + 64, 16);  // h as bf16 (hi, lo) operand words
+  pl.a.off_cc = take(static_cast<size_t>(k) * ngc * 4, 16);
+  pl.a.off_tt = take(static_cast<size_t>(k) * ts * ngc * 8, 16);
+  pl.a.off_ys = take(static_cast<size_t>(k) * ts * ngc * 16 * 4, 16);
   pl.a.off_tab = take(sizeof(t1::Tab), 16);
   pl.a.off_bar = take(8 * (2 + t1::kMaxChunks), 8);
   pl.smem = off;
@@ -421,6 +494,7 @@ bool decode_t1_eligible(const DecodeT1Params& p) {
   // scale groups: powers of two that are multiples of the 32-code chunk
   for (int g : {p.gate.group, p.down.group})
     if (g < 32 || (g & (g - 1)) || g % 32) return false;
+  if (p.down.group % 128) return false;  // one scale per 128-code tensor-core group
   if (p.up.group != p.gate.group || p.up.sstride != p.gate.sstride) return false;
   if (reinterpret_cast<uintptr_t>(p.x) % 16) return false;
   if (p.logits != nullptr && (reinterpret_cast<uintptr_t>(p.logits) % 16 || (p.E * 2) % 16)) return false;
@@ -468,11 +542,13 @@ int launch_decode_t1(const DecodeT1Params& p, cudaStream_t st) {
   cfg.blockDim = dim3(t1::kThreads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   void* args[] = {&a};
   return cudaLaunchKernelExC(&cfg, kern, args) == cudaSuccess ? 1 : -2;
 }

@@ -166,8 +166,12 @@ class MoeLayer:
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_TRACE, int(bool(enabled))), self._h, "moe_set_option")
 
     def read_trace(self, stream=None):
-        """[num_ctas][6] phase timestamps (ns) of the last traced decode launch:
-        entry, routing done, gate/up done, grid barrier passed, h staged, exit."""
+        """[num_ctas][16] phase stamps of the last traced single-token decode launch.
+
+        Column 0 is %globaltimer at CTA entry (ns); columns 1-12 are SM clock cycles since
+        entry: inputs landed, routing done, chunk table built, prologue done, copies
+        requested, own gate/up rows done, h written, grid barrier passed, h staged, down
+        blocks landed, down rows done, exit."""
         import numpy as np
 
         buf = (ctypes.c_uint64 * (1024 * 16))()
