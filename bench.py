@@ -65,6 +65,9 @@ def parse_args():
                     help="config 5: global prefill,decode token counts of the 48-layer expert-parallel stack "
                          "('' = skip)")
     ap.add_argument("--ep-steps", type=int, default=3)
+    ap.add_argument("--trace", action="store_true",
+                    help="after the timed region, record the single-token kernel's per-CTA phase stamps "
+                         "and add their median / slowest-CTA times to the JSON line")
     ap.add_argument("--skip-decode", action="store_true",
                     help="report only the prefill workloads (profiling runs of the grouped GEMM)")
     return ap.parse_args()
@@ -267,6 +270,36 @@ def distinct_experts(layers, logits):
         ids, _ = lay.route(lg)
         out.append(int(torch.unique(ids).numel()))
     return out
+
+
+T1_PHASES = ["inputs landed", "routing done", "chunk table built", "prologue done", "copies queued",
+             "own gate/up rows done", "h written", "grid barrier passed", "h staged", "down blocks landed",
+             "down tiles done", "exit"]
+
+
+def trace_phases(layers, x, logits, outs, sm_mhz, reps=6):
+    """Per-CTA phase stamps of the single-token kernel (SM clock cycles since CTA
+    entry), over `reps` traced passes of the layer cycle, outside any timed region.
+    Returns {phase: [median us, slowest-CTA us]}."""
+    import numpy as np
+    import torch
+
+    L = len(layers)
+    for lay in layers:
+        lay.set_trace(True)
+    rows = []
+    try:
+        for _ in range(reps):
+            for i in range(L):
+                layers[i].forward(x[i], logits[i], out=outs[i])
+            torch.cuda.synchronize()
+            rows.append(layers[L - 1].read_trace().astype(np.int64))
+    finally:
+        for lay in layers:
+            lay.set_trace(False)
+    tr = np.concatenate(rows[1:])
+    return {name: [round(float(np.median(tr[:, i + 1])) / sm_mhz, 3), round(float(tr[:, i + 1].max()) / sm_mhz, 3)]
+            for i, name in enumerate(T1_PHASES)}
 
 
 def run_e2e(layers, x, logits, steps):
@@ -539,6 +572,9 @@ def main():
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }
+
+    if args.trace and fused and args.batch == 1:
+        line["phase_timeline_us"] = trace_phases(layers, x, logits, outs, clk.summary().get("sm_mhz") or 1965.0)
 
     if not args.no_e2e:
         e_ms, h2d, d2h = run_e2e(layers, x, logits, args.e2e_steps)
