@@ -65,6 +65,7 @@ def parse_args():
                     help="config 5: global prefill,decode token counts of the 48-layer expert-parallel stack "
                          "('' = skip)")
     ap.add_argument("--ep-steps", type=int, default=3)
+    ap.add_argument("--no-c1", action="store_true", help="skip the config-1 (W8 per-channel, batch 1) decode line")
     ap.add_argument("--trace", action="store_true",
                     help="after the timed region, record the single-token kernel's per-CTA phase stamps "
                          "and add their median / slowest-CTA times to the JSON line")
@@ -573,6 +574,9 @@ def main():
         "clocks": clk.summary(),
     }
 
+    if not args.no_c1 and args.batch == 1:
+        line["c1_w8_decode_b1"] = run_c1(gen, dev, 48 * 500, 48)
+
     if args.trace and fused and args.batch == 1:
         line["phase_timeline_us"] = trace_phases(layers, x, logits, outs, clk.summary().get("sm_mhz") or 1965.0)
 
@@ -746,6 +750,48 @@ def run_prefill(name: str, gen, device, steps: int, warmup: int):
     del layer, lw, gq, gs, uq, us, dq, ds
     torch.cuda.empty_cache()
     return res
+
+
+def run_c1(gen, device, steps: int, warmup: int, n_layers: int = 6):
+    """Config 1: Qwen3-shaped W8 per-output-channel decode at batch 1 (the
+    single-launch multi-token kernel; the single-token kernel is W4 only).
+    n_layers distinct layers (0.6 GB of expert weights each) are cycled in a
+    CUDA graph, so every step reads its 8 experts (37.8 MB) from HBM."""
+    import torch
+
+    from nano_ktrans_b200 import _lib
+    from nano_ktrans_b200.moe_layer import MoeLayer
+    from nano_ktrans_b200.weights import LayerWeights
+
+    E, H, I, k = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["top_k"]
+    layers, x, logits = [], [], []
+    for _ in range(n_layers):
+        gq, gs = quantized_stack(gen, device, E, I, H, 8, 0)
+        uq, us = quantized_stack(gen, device, E, I, H, 8, 0)
+        dq, ds = quantized_stack(gen, device, E, H, I, 8, 0)
+        lw = LayerWeights(bits=8, group_size=0, gate_q=gq, gate_s=gs, up_q=uq, up_s=us, down_q=dq, down_s=ds)
+        layers.append(MoeLayer(lw, top_k=k, router_use_softmax=True, normalize_topk_prob=True, max_tokens=1))
+        xi = torch.randn(1, H, generator=gen, device=device).to(torch.bfloat16)
+        wr = (torch.randn(E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+        x.append(xi)
+        logits.append(xi @ wr.T)
+    outs = [torch.empty_like(xi) for xi in x]
+    ms, k_ms, launches = run_device(layers, x, logits, outs, steps, warmup, profile_layer_class=_lib.K_DECODE_FUSED)
+    per_expert = 3 * H * I + (2 * I + H) * 2  # int8 codes + one bf16 scale per output row: 4,725,760 B
+    distinct = [int(torch.unique(lay.route(lg)[0]).numel()) for lay, lg in zip(layers, logits)]
+    step_bytes = sum(distinct[i % n_layers] for i in range(steps)) / steps * per_expert
+    peak, peak_kind = hbm_peak()
+    gbs = step_bytes / (ms / steps / 1e3) / 1e9
+    kgbs = step_bytes / (k_ms / 1e3) / 1e9
+    del layers
+    torch.cuda.empty_cache()
+    return {"config": "C1: E=128 H=2048 I=768 top8 renormalised, W8 per-channel, bf16 scales, batch 1",
+            "tokens_per_s": steps / (ms / 1e3), "ms_per_step": ms / steps, "launches_per_step": launches,
+            "expert_weight_gbs": gbs, "expert_weight_frac_of_peak": gbs / peak,
+            "roofline": {"bound": "hbm", "kernel": "moe_decode_fused_kernel<8>", "achieved": kgbs, "peak": peak,
+                         "unit": "GB/s", "frac": kgbs / peak, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": step_bytes, "avg_launch_ms": k_ms},
+            "layers_cycled": n_layers}
 
 
 def prefill_block(args, dev, rank):
