@@ -386,3 +386,40 @@ def test_single_token_decode_repeated_and_masked(cuda_device):
     ref = mo.offload_forward_f32(d["x"], d["ids"], d["w"], d["experts"], mask.astype(bool))
     hp.assert_parity(hp.bf16_bits(part), ref, MAX_ABS, MEAN_REL)
     assert layer.read_status() == 0
+
+
+_T1_SHAPES = {
+    # 7 output rows per CTA, 4 tensor-core groups per down row
+    "h1024": dict(experts=64, top_k=4, hidden=1024, inter=512, use_softmax=True, renormalize=True),
+    # 28 output rows per CTA: two 16-row down tiles, the second one partial
+    "h4096": dict(experts=32, top_k=4, hidden=4096, inter=1024, use_softmax=True, renormalize=True),
+    # 56 output rows per CTA (warps take two combine rows each), Mixtral routing, 16 experts
+    "h8192_mixtral": dict(experts=16, top_k=2, hidden=8192, inter=512, use_softmax=False, renormalize=True),
+}
+
+
+@pytest.mark.parametrize("name", sorted(_T1_SHAPES))
+def test_single_token_decode_shapes(name, cuda_device):
+    """The single-token kernel away from the Qwen3 shape: other row counts per CTA,
+    multi-tile down projections and both routing modes, against the oracle and
+    the multi-kernel chain."""
+    cfg = _T1_SHAPES[name]
+    d = _full_case(cfg, 1, 4, 128, 90, cuda_device)
+    layer = d["layer"]
+    x = hp.bf16_tensor(d["x"], cuda_device)
+    lg = hp.bf16_tensor(d["logits"], cuda_device)
+    k = cfg["top_k"]
+    ids_f = torch.empty(1, k, dtype=torch.int64, device=cuda_device)
+    w_f = torch.empty(1, k, dtype=torch.bfloat16, device=cuda_device)
+    layer.set_decode_fused(1)
+    fused = layer.forward(x, lg, out_ids=ids_f, out_weights=w_f).clone()
+    assert layer.last_launch_count() == 1
+    torch.cuda.synchronize()
+    assert mo.tie_aware_match(ids_f.cpu().numpy(), d["ids"], d["ranked"]).all()
+    layer.set_decode_fused(0)
+    chain = layer.forward(x, lg)
+    torch.cuda.synchronize()
+    hp.assert_paths_agree(hp.bf16_bits(fused), hp.bf16_bits(chain), MAX_ABS, MEAN_REL)
+    ref = mo.offload_forward_f32(d["x"], ids_f.cpu().numpy(), hp.bf16_bits(w_f), d["experts"])
+    hp.assert_parity(hp.bf16_bits(fused), ref, MAX_ABS, MEAN_REL)
+    assert layer.read_status() == 0
