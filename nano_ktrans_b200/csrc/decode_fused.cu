@@ -684,11 +684,7 @@ int launch_decode_fused(int bits, const DecodeFusedParams& p, cudaStream_t st) {
 
   void* kern = bits == 4 ? (tok == 1 ? pick_epl<4, 1>(p.E) : pick_epl<4, 4>(p.E))
                          : (tok == 1 ? pick_epl<8, 1>(p.E) : pick_epl<8, 4>(p.E));
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
-    return -1;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFThreads, smem) != cudaSuccess || per_sm < 1)
-    return -1;
+  if (!ensure_dynamic_smem(kern, smem, kFThreads)) return -1;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kFThreads);

@@ -530,13 +530,7 @@ int launch_decode_t1(const DecodeT1Params& p, cudaStream_t st) {
   a.trace = p.trace;
   a.status = p.status;
   void* kern = p.E <= 32 ? t1_kernel<1>() : p.E <= 64 ? t1_kernel<2>() : p.E <= 128 ? t1_kernel<4>() : t1_kernel<8>();
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem)) !=
-      cudaSuccess)
-    return -1;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, t1::kThreads, pl.smem) != cudaSuccess ||
-      per_sm < 1)
-    return -1;
+  if (!ensure_dynamic_smem(kern, pl.smem, t1::kThreads)) return -1;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(p.num_sms);
   cfg.blockDim = dim3(t1::kThreads);

@@ -94,6 +94,10 @@ struct DecodeT1Params {
   int* status;
   int num_sms;
 };
+// Dynamic shared-memory opt-in + one-CTA-per-SM check, done once per (kernel,
+// device) and new maximum size (launch_util.cu).
+bool ensure_dynamic_smem(const void* kern, size_t smem, int threads);
+
 bool decode_t1_eligible(const DecodeT1Params& p);
 // 1 = launched; negative = not launched.
 int launch_decode_t1(const DecodeT1Params& p, cudaStream_t st);
