@@ -48,7 +48,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxK = 32;        // routed experts of the token
 constexpr int kChunkRows = 8;    // phase-2 rows per bulk-copy chunk
 constexpr int kMaxChunks = 40;
-constexpr int kRowsC = 64;       // phase-5 rows per CTA
+constexpr int kRowsC = 64;       // most phase-5 output rows per CTA
 
 struct Args {
   const uint16_t* x;
@@ -63,7 +63,7 @@ struct Args {
   float* hbuf;  // [k][I]
   uint16_t* out;
   unsigned long long* bar;
-  unsigned long long* trace;  // [G][16] %globaltimer stamps, or null
+  unsigned long long* trace;  // [G][16] phase stamps (see T1_TRACE), or null
   int* status;
   // dynamic shared-memory carve-up (byte offsets)
   int off_lg, off_x, off_xq, off_corr, off_b, off_c, off_sb, off_sc, off_act, off_cc, off_tt, off_ys, off_tab, off_bar;
