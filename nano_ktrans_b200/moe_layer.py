@@ -41,6 +41,7 @@ class MoeLayer:
         self.router_use_softmax = bool(router_use_softmax)
         self.normalize_topk_prob = bool(normalize_topk_prob)
         self.max_tokens = int(max_tokens)
+        self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         L = _lib.lib()
         desc = _lib.MoeLayerDesc(self.num_experts, self.top_k, self.hidden_size, self.inter_size, weights.bits,
                                  weights.group_size, int(self.router_use_softmax), int(self.normalize_topk_prob),
@@ -83,9 +84,19 @@ class MoeLayer:
     def _check_tokens(self, x: torch.Tensor) -> int:
         if x.dim() != 2 or x.shape[1] != self.hidden_size:
             raise ValueError(f"expected [T, {self.hidden_size}] activations, got {tuple(x.shape)}")
-        if x.dtype != torch.bfloat16 or x.device != self.device:
+        if x.dtype is not torch.bfloat16 or not x.is_cuda or x.get_device() != self._dev_index:
             raise ValueError(f"activations must be bf16 on {self.device}")
         return int(x.shape[0])
+
+    def _out_for(self, xc: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
+        """The caller's output buffer after checking that the kernels may write
+        [T, H] bf16 into it, or a new one."""
+        if out is None:
+            return torch.empty_like(xc)
+        if (out.shape != xc.shape or out.dtype is not torch.bfloat16 or not out.is_cuda
+                or out.get_device() != self._dev_index or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous bf16 {tuple(xc.shape)} tensor on {self.device}")
+        return out
 
     def route(self, router_logits: torch.Tensor, *, out_ids=None, out_weights=None, stream=None):
         t = int(router_logits.shape[0])
@@ -115,7 +126,7 @@ class MoeLayer:
         mask = None
         if offload_mask is not None:
             mask = offload_mask.to(device=self.device, dtype=torch.uint8).contiguous()
-        out = out if out is not None else torch.empty_like(xc)
+        out = self._out_for(xc, out)
         _lib.check(_lib.lib().moe_experts_forward(self._h, xc.data_ptr(), ids.data_ptr(), w.data_ptr(), t,
                                                   _ptr(mask), int(add_shared), out.data_ptr(),
                                                   _stream_handle(stream)), self._h, "moe_experts_forward")
@@ -124,10 +135,10 @@ class MoeLayer:
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor, *, out=None, out_ids=None, out_weights=None,
                 stream=None) -> torch.Tensor:
         t = self._check_tokens(x)
-        if router_logits.dtype != torch.bfloat16 or tuple(router_logits.shape) != (t, self.num_experts):
+        if router_logits.dtype is not torch.bfloat16 or router_logits.shape != (t, self.num_experts):
             raise ValueError("router logits must be bf16 [T, E]")
         xc, lc = x.contiguous(), router_logits.contiguous()
-        out = out if out is not None else torch.empty_like(xc)
+        out = self._out_for(xc, out)
         _lib.check(_lib.lib().moe_forward(self._h, xc.data_ptr(), lc.data_ptr(), t, out.data_ptr(), _ptr(out_ids),
                                           _ptr(out_weights), _stream_handle(stream)), self._h, "moe_forward")
         return out

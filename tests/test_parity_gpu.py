@@ -423,3 +423,21 @@ def test_single_token_decode_shapes(name, cuda_device):
     ref = mo.offload_forward_f32(d["x"], ids_f.cpu().numpy(), hp.bf16_bits(w_f), d["experts"])
     hp.assert_parity(hp.bf16_bits(fused), ref, MAX_ABS, MEAN_REL)
     assert layer.read_status() == 0
+
+
+def test_forward_rejects_unsafe_output_buffers(cuda_device):
+    """A caller's out buffer is checked before any kernel may write [T, H] bf16 into it."""
+    d = _full_case(hp.QWEN3, 2, 4, 128, 5, cuda_device)
+    layer = d["layer"]
+    x = hp.bf16_tensor(d["x"], cuda_device)
+    lg = hp.bf16_tensor(d["logits"], cuda_device)
+    H = hp.QWEN3["hidden"]
+    bad = [torch.empty(1, H, dtype=torch.bfloat16, device=cuda_device),        # too few rows
+           torch.empty(2, H, dtype=torch.float32, device=cuda_device),         # wrong dtype
+           torch.empty(H, 2, dtype=torch.bfloat16, device=cuda_device).t(),    # not contiguous
+           torch.empty(2, H, dtype=torch.bfloat16)]                            # host memory
+    for out in bad:
+        with pytest.raises(ValueError):
+            layer.forward(x, lg, out=out)
+    good = torch.empty(2, H, dtype=torch.bfloat16, device=cuda_device)
+    assert layer.forward(x, lg, out=good) is good
