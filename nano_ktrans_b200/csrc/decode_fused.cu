@@ -30,10 +30,10 @@
 // Every wait is bounded: on expiry the kernel records kStatusTimeout in the
 // status word, stops computing, drains its outstanding copies (bounded) and
 // still arrives at the grid barrier, so no other CTA waits on it.
-#include <cuda/atomic>
 
 #include <algorithm>
 
+#include "async_copy.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "route_warp.cuh"
@@ -48,7 +48,6 @@ constexpr int kFMaxStages = 96;     // stage descriptors per CTA
 constexpr int kFRowsC = 64;         // phase-C rows per CTA (16 warps x 4 rows)
 constexpr int kFMaxPairs = 32;      // (token, expert) pairs per launch
 constexpr int kFMaxExpC = 8;        // experts per phase-C stage
-constexpr uint32_t kSpinLimit = 1u << 22;
 
 struct FusedArgs {
   const uint16_t* x;
@@ -94,71 +93,15 @@ struct Tables {
   int n_act, n_pairs, n_stages, n_ring, abort;
 };
 
-// --------------------------------------------------------------------------
-// TMA / mbarrier / barrier primitives
-// --------------------------------------------------------------------------
-
-MOE_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-MOE_DEV void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-MOE_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-MOE_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-MOE_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-
-MOE_DEV void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
-
-// Grid-wide barrier for a cooperative launch.  The 64-bit arrival counter
-// only grows: a CTA's arrival returns n, its launch's barrier is complete
-// when the counter reaches (n / G + 1) * G.  No reset, no second atomic.
-// Returns false if the wait hit its iteration limit.
-MOE_DEV bool grid_sync_bounded(unsigned long long* bar, int* ok_smem) {
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> count(*bar);
-    const unsigned long long g = gridDim.x;
-    const unsigned long long target = (count.fetch_add(1ull, cuda::memory_order_acq_rel) / g + 1) * g;
-    int ok = 1;
-    for (uint32_t i = 0; count.load(cuda::memory_order_acquire) < target; ++i) {
-      if (i > kSpinLimit) {
-        ok = 0;
-        break;
-      }
-    }
-    *ok_smem = ok;
-  }
-  __syncthreads();
-  return *ok_smem != 0;
-}
-
-MOE_DEV unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+// mbarrier, bulk-copy and grid-barrier primitives: async_copy.cuh
+using ac::bulk_g2s;
+using ac::global_ns;
+using ac::grid_sync_bounded;
+using ac::mbar_init;
+using ac::mbar_try_wait;
+using ac::mbar_wait_bounded;
+using ac::smem_u32;
+MOE_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) { ac::mbar_arrive_expect_tx(bar, bytes); }
 
 // Phase timestamps (thread 0 of each CTA), when tracing is on: 0 entry,
 // 1 routing and stage list done, 2 phase B done, 3 grid barrier passed,
