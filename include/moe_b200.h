@@ -200,8 +200,8 @@ enum moe_option {
    * kernel); 2: the multi-token kernel also for T == 1; 0: always use the
    * multi-kernel path. */
   MOE_OPT_DECODE_FUSED = 1,
-  /* 1: the single-launch decode kernel records per-CTA phase timestamps
-   * (allocates num_SMs * 8 * 8 bytes); read them with moe_read_trace. */
+  /* 1: the single-launch decode kernels record per-CTA phase stamps
+   * (allocates num_SMs * 16 * 8 bytes); read them with moe_read_trace. */
   MOE_OPT_TRACE = 2,
   /* Expert projections of the multi-kernel path: 0 = matvec kernels only;
    * 1 (default) = tensor-core grouped GEMM once T * top_k >= 4 * num_experts;
@@ -216,11 +216,15 @@ enum moe_option {
   MOE_OPT_GEMM_TILE = 4
 };
 
-/* Copy the phase timestamps of the last traced single-launch decode step:
- * out[c * 8 + i] = %globaltimer (ns) of CTA c at phase i (0 entry, 1 routing
- * done, 2 gate/up done, 3 grid barrier passed, 4 intermediate staged, 5 exit).
- * *n receives the CTA count.  Synchronises `stream`.  (No counterpart in the
- * reference: tracing support.) */
+/* Copy the phase stamps of the last traced single-launch decode step, 16 per
+ * CTA: out[c * 16 + i].  Single-token kernel (T == 1): slot 0 = %globaltimer
+ * (ns) at CTA entry, slots 1-12 = SM clock cycles since entry at: inputs
+ * landed, routing done, chunk table built, prologue done, copies queued, own
+ * gate/up rows done, h written, grid barrier passed, h staged, down blocks
+ * landed, down tiles done, exit.  Multi-token kernel: slots 0-5 =
+ * %globaltimer (ns) at entry, routing done, gate/up done, grid barrier
+ * passed, intermediate staged, exit.  *n receives the CTA count.
+ * Synchronises `stream`.  (No counterpart in the reference: tracing support.) */
 int moe_read_trace(void* handle, uint64_t* out, int32_t max_entries, int32_t* n, void* stream);
 
 /* Set a handle option (no counterpart in the reference: selects between two
