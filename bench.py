@@ -790,7 +790,8 @@ def run_c1(gen, device, steps: int, warmup: int, n_layers: int = 6):
             "expert_weight_gbs": gbs, "expert_weight_frac_of_peak": gbs / peak,
             "roofline": {"bound": "hbm", "kernel": "moe_decode_fused_kernel<8>", "achieved": kgbs, "peak": peak,
                          "unit": "GB/s", "frac": kgbs / peak, "peak_source": peak_kind,
-                         "algorithmic_bytes_per_launch": step_bytes, "avg_launch_ms": k_ms},
+                         "algorithmic_bytes_per_launch": step_bytes, "avg_launch_ms": k_ms,
+                         "traffic": read_traffic("decode_fused_w8", 1)},
             "layers_cycled": n_layers}
 
 
