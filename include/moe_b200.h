@@ -252,16 +252,20 @@ void moe_destroy(void* handle);
  *   - The caller passes the layer description, the device weight pointers
  *     (layout as for moe_set_weights), x [T, H] and logits [T, E] (bf16), and
  *     the outputs out [T, H] (bf16), topk_ids [T, k] (int64), topk_weights
- *     [T, k] (bf16); status_dev (nullable) receives the device status bits
- *     (see moe_read_status).
+ *     [T, k] (bf16).  status_dev receives the device status bits (see
+ *     moe_read_status): pass a zeroed int32, the bits accumulate until the
+ *     caller clears them; NULL discards them (timeouts and bad ids then go
+ *     unreported).
  *   - Scratch is one file-scope device array per GPU that loads the library:
- *     T * top_k * inter_size must be <= 65536 floats, and the batch must fit
- *     the single-launch kernel (T <= 4, T * top_k <= 32, E <= 256); larger
- *     calls return MOE_ERANGE with a message and launch nothing.
+ *     T * top_k * inter_size must be <= 24576 floats (96 KiB), and the batch
+ *     must fit the single-launch kernel (T <= 4, T * top_k <= 32, E <= 256);
+ *     larger calls return MOE_ERANGE with a message and launch nothing.
  *   - Every call on a device shares that array: calls whose kernels overlap
  *     on the GPU race and give wrong results; serialise them.
  *   - The first call on a device looks up the array's address
- *     (cudaGetSymbolAddress); make it outside any stream capture.
+ *     (cudaGetSymbolAddress); make it outside any stream capture.  The
+ *     address is kept for the life of the process, so the entry point must
+ *     not be used after cudaDeviceReset.
  * err/err_len receive a message on failure. */
 int moe_decode_noalloc(const moe_layer_desc* desc, const moe_weights* w, const uint16_t* x_dev,
                        const uint16_t* logits_dev, int32_t num_tokens, uint16_t* out_dev,

@@ -2,14 +2,17 @@
 
 Usage: ``python -m nano_ktrans_b200.build [--verbose]``.  Object files go to
 ``nano_ktrans_b200/_build/``; the shared library lands next to this file so it
-travels with the source tree.  Rebuilds only when a source is newer than the
-library.
+travels with the source tree.  The library is rebuilt whenever the SHA-256 of
+its sources, headers and compiler flags differs from the digest recorded
+beside it when it was built (``libmoe_b200.so.srchash``): a library built from
+other sources is never reused, whatever the file times say.
 """
 from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
 import glob
+import hashlib
 import os
 import shutil
 import subprocess
@@ -41,11 +44,25 @@ def _deps() -> list[str]:
         glob.glob(os.path.join(INCLUDE, "*.h"))
 
 
+STAMP = LIB + ".srchash"
+
+
+def source_digest() -> str:
+    """SHA-256 over the compiler flags and every source and header, by name and content."""
+    h = hashlib.sha256()
+    h.update(" ".join(ARCH + FLAGS[:-1]).encode())  # the include path itself is machine-specific
+    for p in sorted(_deps()):
+        h.update(os.path.relpath(p, os.path.dirname(PKG)).encode())
+        with open(p, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(STAMP):
         return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(p) <= t for p in _deps())
+    with open(STAMP) as f:
+        return f.read().strip() == source_digest()
 
 
 def build(verbose: bool = False, force: bool = False, ptxas_info: bool = False) -> str:
@@ -77,6 +94,8 @@ def build(verbose: bool = False, force: bool = False, ptxas_info: bool = False) 
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stderr}")
     os.replace(tmp, LIB)
+    with open(STAMP, "w") as f:
+        f.write(source_digest() + "\n")
     return LIB
 
 

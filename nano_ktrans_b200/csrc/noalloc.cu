@@ -13,8 +13,9 @@
 //
 // Limits and sharing:
 //   * scratch holds at most kNoAllocMaxH floats of intermediate:
-//     num_tokens * top_k * inter_size <= kNoAllocMaxH; larger calls are
-//     rejected with MOE_ERANGE before anything is launched;
+//     num_tokens * top_k * inter_size <= kNoAllocMaxH (24576 floats = 96 KiB,
+//     the most the single-launch kernel stages); larger calls are rejected
+//     with MOE_ERANGE before anything is launched;
 //   * the batch must also fit the single-launch kernel (at most 4 tokens and
 //     32 (token, expert) pairs, at most 256 experts);
 //   * every call on a device uses the same array, which keeps the previous
@@ -25,6 +26,12 @@
 //     threads) race on the array and produce wrong results; serialise them.
 //   * the first call on each device looks up the array's device address with
 //     cudaGetSymbolAddress; make that first call outside any stream capture.
+//     The address is remembered per device ordinal for the life of the
+//     process: after cudaDeviceReset (which unloads the module) this entry
+//     point must not be used again in the process;
+//   * a null status_dev discards the kernel's status bits (bounded-wait
+//     timeouts, bad expert ids); pass a zeroed int32 to receive them - bits
+//     accumulate across calls until the caller clears the word.
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -37,7 +44,7 @@
 
 namespace {
 
-constexpr size_t kNoAllocMaxH = 65536;  // floats of SiLU(gate)*up intermediate (256 KiB)
+constexpr size_t kNoAllocMaxH = 24576;  // floats of SiLU(gate)*up intermediate (96 KiB, the kernel's cap)
 constexpr size_t kNoAllocHeader = 256;  // barrier counter (8 B) + status word (4 B), padded
 constexpr size_t kNoAllocBytes = kNoAllocHeader + kNoAllocMaxH * sizeof(float);
 constexpr int kMaxDevices = 64;
@@ -139,8 +146,12 @@ extern "C" int moe_decode_noalloc(const moe_layer_desc* desc, const moe_weights*
     return MOE_ERANGE;
   }
   int num_sms = 0, dev = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce == cudaSuccess) ce = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (ce != cudaSuccess || num_sms < 1) {
+    put_err(err, err_len, "moe_decode_noalloc: device query failed: %s", cudaGetErrorString(ce));
+    return MOE_ECUDA;
+  }
   moe::DecodeFusedParams p{};
   p.gate = proj(d, w->gate_q_dev, w->gate_s_dev, d.inter_size, d.hidden_size);
   p.up = proj(d, w->up_q_dev, w->up_s_dev, d.inter_size, d.hidden_size);

@@ -241,9 +241,19 @@ class EpMoeLayer(EpStep):
         self._send_local = torch.empty(self.max_tokens * self.top_k, dtype=torch.int64, device=self.device)
         self._local_ids = torch.arange(self.epr, dtype=torch.int64, device=self.device).repeat(self.world)
 
+    # -- argument checks: every tensor whose pointer reaches a kernel ----------
+    def _check(self, t: torch.Tensor, name: str, shape, dtype) -> None:
+        if (tuple(t.shape) != tuple(shape) or t.dtype is not dtype or not t.is_cuda
+                or t.get_device() != self.slot_of_expert.get_device()):
+            raise ValueError(f"{name} must be {dtype} {list(shape)} on {self.device}, got "
+                             f"{t.dtype} {list(t.shape)} on {t.device}")
+
     # -- phases -------------------------------------------------------------
     def route(self, logits: torch.Tensor, stream=None):
+        if logits.dim() != 2:
+            raise ValueError("router logits must be [T, E]")
         t = int(logits.shape[0])
+        self._check(logits, "router logits", (t, self.num_experts), torch.bfloat16)
         ids = torch.empty(t, self.top_k, dtype=torch.int64, device=self.device)
         w = torch.empty(t, self.top_k, dtype=torch.bfloat16, device=self.device)
         _lib.check(_lib.lib().moe_route(self.router._h, logits.contiguous().data_ptr(), t, ids.data_ptr(),
@@ -251,9 +261,15 @@ class EpMoeLayer(EpStep):
         return ids, w
 
     def dispatch(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, stream=None) -> DispatchState:
+        if x.dim() != 2:
+            raise ValueError("activations must be [T, H]")
         t = int(x.shape[0])
         if t > self.max_tokens:
             raise ValueError(f"{t} tokens above max_tokens {self.max_tokens}")
+        self._check(x, "activations", (t, self.hidden), torch.bfloat16)
+        self._check(ids, "topk_ids", (t, self.top_k), torch.int64)
+        self._check(w, "topk_weights", (t, self.top_k), torch.bfloat16)
+        ids, w = ids.contiguous(), w.contiguous()
         send_rows = torch.empty(t * self.top_k, self.hidden, dtype=torch.bfloat16, device=self.device)
         counts = torch.empty(self.num_experts, dtype=torch.int32, device=self.device)
         _lib.check(_lib.lib().moe_ep_dispatch(self.router._h, x.contiguous().data_ptr(), ids.data_ptr(), t,
@@ -279,6 +295,10 @@ class EpMoeLayer(EpStep):
 
     def combine(self, st: DispatchState, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
         t = int(st.ids.shape[0])
+        if out is not None:
+            self._check(out, "out", (t, self.hidden), torch.bfloat16)
+            if not out.is_contiguous():
+                raise ValueError("out must be contiguous")
         out = out if out is not None else torch.empty(t, self.hidden, dtype=torch.bfloat16, device=self.device)
         if t:
             _lib.check(_lib.lib().moe_ep_combine(self.router._h, st.ids.data_ptr(), st.weights.data_ptr(), t,

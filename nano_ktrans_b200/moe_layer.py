@@ -81,27 +81,49 @@ class MoeLayer:
             pass
 
     # ------------------------------------------------------------------
+    # Argument checks.  Every tensor whose pointer reaches a kernel is checked
+    # for device, dtype, exact shape and contiguity first: a wrong buffer must
+    # raise here, never be handed to the device as a raw pointer.
+    def _on_device(self, t: torch.Tensor) -> bool:
+        return t.is_cuda and t.get_device() == self._dev_index
+
     def _check_tokens(self, x: torch.Tensor) -> int:
         if x.dim() != 2 or x.shape[1] != self.hidden_size:
             raise ValueError(f"expected [T, {self.hidden_size}] activations, got {tuple(x.shape)}")
-        if x.dtype is not torch.bfloat16 or not x.is_cuda or x.get_device() != self._dev_index:
+        if x.dtype is not torch.bfloat16 or not self._on_device(x):
             raise ValueError(f"activations must be bf16 on {self.device}")
         return int(x.shape[0])
+
+    def _check_logits(self, logits: torch.Tensor, t: Optional[int] = None) -> int:
+        if logits.dim() != 2 or logits.shape[1] != self.num_experts or (t is not None and logits.shape[0] != t):
+            raise ValueError(f"router logits must be [T, {self.num_experts}], got {tuple(logits.shape)}")
+        if logits.dtype is not torch.bfloat16 or not self._on_device(logits):
+            raise ValueError(f"router logits must be bf16 on {self.device}")
+        return int(logits.shape[0])
+
+    def _check_routing_out(self, t: int, out_ids, out_weights) -> None:
+        """Caller-provided routing outputs: exactly [T, top_k], int64 ids and bf16 weights,
+        contiguous, on this device (the kernels write T * top_k entries into each)."""
+        for buf, dt, name in ((out_ids, torch.int64, "out_ids"), (out_weights, torch.bfloat16, "out_weights")):
+            if buf is None:
+                continue
+            if (tuple(buf.shape) != (t, self.top_k) or buf.dtype is not dt or not self._on_device(buf)
+                    or not buf.is_contiguous()):
+                raise ValueError(f"{name} must be a contiguous {dt} [{t}, {self.top_k}] tensor on {self.device}")
 
     def _out_for(self, xc: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
         """The caller's output buffer after checking that the kernels may write
         [T, H] bf16 into it, or a new one."""
         if out is None:
             return torch.empty_like(xc)
-        if (out.shape != xc.shape or out.dtype is not torch.bfloat16 or not out.is_cuda
-                or out.get_device() != self._dev_index or not out.is_contiguous()):
+        if (out.shape != xc.shape or out.dtype is not torch.bfloat16 or not self._on_device(out)
+                or not out.is_contiguous()):
             raise ValueError(f"out must be a contiguous bf16 {tuple(xc.shape)} tensor on {self.device}")
         return out
 
     def route(self, router_logits: torch.Tensor, *, out_ids=None, out_weights=None, stream=None):
-        t = int(router_logits.shape[0])
-        if router_logits.dtype != torch.bfloat16 or router_logits.shape[1] != self.num_experts:
-            raise ValueError("router logits must be bf16 [T, E]")
+        t = self._check_logits(router_logits)
+        self._check_routing_out(t, out_ids, out_weights)
         logits = router_logits.contiguous()
         ids = out_ids if out_ids is not None else torch.empty(t, self.top_k, dtype=torch.int64, device=self.device)
         w = out_weights if out_weights is not None else torch.empty(t, self.top_k, dtype=torch.bfloat16,
@@ -114,6 +136,8 @@ class MoeLayer:
                         offload_mask: Optional[torch.Tensor] = None, add_shared: bool = False, out=None,
                         stream=None) -> torch.Tensor:
         t = self._check_tokens(x)
+        if not self._on_device(topk_ids) or not self._on_device(topk_weights):
+            raise ValueError(f"routing tensors must be on {self.device}")
         ids = topk_ids
         if ids.dtype != torch.int64:
             ids = ids.to(torch.int64)
@@ -125,7 +149,9 @@ class MoeLayer:
             raise ValueError(f"routing tensors must be [{t}, {self.top_k}]")
         mask = None
         if offload_mask is not None:
-            mask = offload_mask.to(device=self.device, dtype=torch.uint8).contiguous()
+            if offload_mask.numel() != self.num_experts:
+                raise ValueError(f"offload_mask must hold {self.num_experts} entries")
+            mask = offload_mask.reshape(-1).to(device=self.device, dtype=torch.uint8).contiguous()
         out = self._out_for(xc, out)
         _lib.check(_lib.lib().moe_experts_forward(self._h, xc.data_ptr(), ids.data_ptr(), w.data_ptr(), t,
                                                   _ptr(mask), int(add_shared), out.data_ptr(),
@@ -135,8 +161,8 @@ class MoeLayer:
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor, *, out=None, out_ids=None, out_weights=None,
                 stream=None) -> torch.Tensor:
         t = self._check_tokens(x)
-        if router_logits.dtype is not torch.bfloat16 or router_logits.shape != (t, self.num_experts):
-            raise ValueError("router logits must be bf16 [T, E]")
+        self._check_logits(router_logits, t)
+        self._check_routing_out(t, out_ids, out_weights)
         xc, lc = x.contiguous(), router_logits.contiguous()
         out = self._out_for(xc, out)
         _lib.check(_lib.lib().moe_forward(self._h, xc.data_ptr(), lc.data_ptr(), t, out.data_ptr(), _ptr(out_ids),

@@ -162,3 +162,56 @@ def test_routing_oracle_properties():
     np.testing.assert_allclose(wf.sum(1), 1.0, atol=2e-2)
     ids2, w2, _ = mo.route(logits, 2, False, True)
     np.testing.assert_allclose(mo.bf16_bits_to_f32(w2).sum(1), 1.0, atol=1e-2)
+
+
+def _stub_layer():
+    """A MoeLayer with the attributes the argument checks read and no handle
+    (the checks must reject before anything reaches the library)."""
+    from nano_ktrans_b200.moe_layer import MoeLayer
+
+    lay = MoeLayer.__new__(MoeLayer)
+    lay.device, lay._dev_index, lay._h = torch.device("cuda", 0), 0, None
+    lay.num_experts, lay.top_k, lay.hidden_size = 8, 2, 64
+    return lay
+
+
+def test_moe_layer_rejects_host_tensors_before_any_launch():
+    lay = _stub_layer()
+    x = torch.zeros(3, 64, dtype=torch.bfloat16)
+    lg = torch.zeros(3, 8, dtype=torch.bfloat16)
+    for call in (lambda: lay.route(lg), lambda: lay.forward(x, lg),
+                 lambda: lay.experts_forward(x, torch.zeros(3, 2, dtype=torch.int64),
+                                             torch.zeros(3, 2, dtype=torch.bfloat16))):
+        with pytest.raises(ValueError, match="cuda"):
+            call()
+
+
+@pytest.mark.parametrize("which", ["ids_shape", "ids_dtype", "ids_strided", "w_shape", "w_dtype", "logits_dtype",
+                                   "logits_rank", "logits_rows"])
+def test_moe_layer_rejects_bad_routing_buffers(which, monkeypatch):
+    """Every routing buffer a kernel writes or reads is checked for exact shape,
+    dtype and contiguity (device placement is taken as given here, no GPU)."""
+    from nano_ktrans_b200.moe_layer import MoeLayer
+
+    monkeypatch.setattr(MoeLayer, "_on_device", lambda self, t: True)
+    lay = _stub_layer()
+    x = torch.zeros(3, 64, dtype=torch.bfloat16)
+    lg = torch.zeros(3, 8, dtype=torch.bfloat16)
+    ids = torch.zeros(3, 2, dtype=torch.int64)
+    w = torch.zeros(3, 2, dtype=torch.bfloat16)
+    bad = {"ids_shape": dict(out_ids=torch.zeros(2, 2, dtype=torch.int64)),
+           "ids_dtype": dict(out_ids=torch.zeros(3, 2, dtype=torch.int32)),
+           "ids_strided": dict(out_ids=torch.zeros(2, 3, dtype=torch.int64).t()),
+           "w_shape": dict(out_weights=torch.zeros(3, 3, dtype=torch.bfloat16)),
+           "w_dtype": dict(out_weights=torch.zeros(3, 2, dtype=torch.float32)),
+           "logits_dtype": dict(logits=lg.float()),
+           "logits_rank": dict(logits=lg.reshape(-1)),
+           "logits_rows": dict(logits=torch.zeros(4, 8, dtype=torch.bfloat16))}[which]
+    logits = bad.pop("logits", lg)
+    kw = dict(out_ids=ids, out_weights=w)
+    kw.update(bad)
+    with pytest.raises(ValueError):
+        lay.forward(x, logits, **kw)
+    if "logits" not in which:
+        with pytest.raises(ValueError):
+            lay.route(lg, **kw)
