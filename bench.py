@@ -65,6 +65,8 @@ def parse_args():
                     help="config 5: global prefill,decode token counts of the 48-layer expert-parallel stack "
                          "('' = skip)")
     ap.add_argument("--ep-steps", type=int, default=3)
+    ap.add_argument("--m32", type=int, default=200,
+                    help="steps of the dense bf16 stacked-bmm batch-1 comparator (0 = skip)")
     ap.add_argument("--no-c1", action="store_true", help="skip the config-1 (W8 per-channel, batch 1) decode line")
     ap.add_argument("--trace", action="store_true",
                     help="after the timed region, record the single-token kernel's per-CTA phase stamps "
@@ -303,11 +305,15 @@ def trace_phases(layers, x, logits, outs, sm_mhz, reps=6):
             for i, name in enumerate(T1_PHASES)}
 
 
-def run_e2e(layers, x, logits, steps):
-    """Public API with host buffers: H2D inputs, MoeLayer.forward, D2H output."""
+def run_e2e(layers, x, logits, steps, call=None):
+    """Public API with host buffers: H2D inputs, MoeLayer.forward (or
+    call(j, x, logits, out)), D2H output."""
     import torch
 
     L = len(layers)
+    if call is None:
+        def call(j, xj, lj, oj):
+            layers[j].forward(xj, lj, out=oj)
     xh = x.cpu().pin_memory()
     lh = logits.cpu().pin_memory()
     oh = torch.empty_like(xh).pin_memory()
@@ -317,7 +323,7 @@ def run_e2e(layers, x, logits, steps):
         j = i % L
         xd[j].copy_(xh[j], non_blocking=True)
         ld[j].copy_(lh[j], non_blocking=True)
-        layers[j].forward(xd[j], ld[j], out=od[j])
+        call(j, xd[j], ld[j], od[j])
         oh[j].copy_(od[j], non_blocking=True)
     torch.cuda.synchronize()
     if torch.distributed.is_initialized():
@@ -329,7 +335,7 @@ def run_e2e(layers, x, logits, steps):
         j = i % L
         xd[j].copy_(xh[j], non_blocking=True)
         ld[j].copy_(lh[j], non_blocking=True)
-        layers[j].forward(xd[j], ld[j], out=od[j])
+        call(j, xd[j], ld[j], od[j])
         oh[j].copy_(od[j], non_blocking=True)
     e1.record(st)
     torch.cuda.synchronize()
@@ -342,6 +348,22 @@ def run_e2e(layers, x, logits, steps):
 # ---------------------------------------------------------------------------
 # CPU (reference algorithm) timing
 # ---------------------------------------------------------------------------
+
+
+def hybrid_layers(lws, device):
+    """HybridMoE layers (the reference's layer class and forward contract) over
+    the same weights, every expert offloaded to the cuda backend."""
+    import torch
+    from torch import nn
+
+    from nano_ktrans_b200.hybrid_moe import HybridMoE
+
+    E, H, I, k = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["top_k"]
+    return [HybridMoE(num_experts=E, top_k=k, hidden_size=H, moe_intermediate_size=I, gpu_experts=nn.ModuleDict(),
+                      gpu_experts_mask=torch.zeros(E, dtype=torch.bool), layer_idx=j, weight_path="",
+                      router_use_softmax=True, normalize_topk_prob=True,
+                      offload_backend_kwargs={"layer_weights": lw, "device": device, "max_tokens": 1})
+            for j, lw in enumerate(lws)]
 
 
 def blas_threads() -> int:
@@ -461,6 +483,15 @@ def main_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    # every host core, also under torch.distributed.run (which sets OMP_NUM_THREADS=1)
+    ncores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(ncores)
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=ncores)
+    except Exception:
+        pass
     torch.manual_seed(args.seed)
     gen = torch.Generator().manual_seed(args.seed)
     from nano_ktrans_b200.weights import quantize_symmetric
@@ -496,7 +527,7 @@ def main_reference(args):
     v = done * args.batch / busy
     cores = blas_threads()
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+        "impl": "reference", "host_cores": ncores, "torch_threads": torch.get_num_threads(), "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "steps_run": done, "warmup": args.warmup, "ms_per_step": 1000 * busy / done,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_block(args, 1),
@@ -555,7 +586,13 @@ def main():
     # roofline: the kernel's algorithmic bytes per launch (codes + scales of the
     # distinct routed experts it reads) / its CUDA-event duration
     per_launch = statistics.mean(d * ((gu_bytes + dn_bytes) if fused else gu_bytes) for d in distinct)
-    achieved = per_launch / (k_ms / 1e3) / 1e9
+    # kernel time of the roofline: with one launch per step (the single-launch
+    # kernel) it is the graph-replay step time itself, measured without anything
+    # inserted between the launches; the event-bracketed replay (which breaks the
+    # programmatic-dependent-launch overlap) is reported beside it, not used
+    one_launch = fused and launches == 1
+    kern_ms = ms / args.steps if one_launch else k_ms
+    achieved = per_launch / (kern_ms / 1e3) / 1e9
     kname = ("moe_decode_t1_kernel" if args.batch == 1 else "moe_decode_fused_kernel<4>") if fused \
         else "expert_matvec_kernel<4,32,gate/up>"
     traffic = read_traffic(("decode_t1" if args.batch == 1 else "decode_fused") if fused else "gateup", args.batch)
@@ -569,13 +606,21 @@ def main():
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
                      "traffic": traffic, "algorithmic_bytes_per_launch": per_launch,
-                     "avg_launch_ms": k_ms},
+                     "avg_launch_ms": kern_ms,
+                     "kernel_time_source": ("graph-replay step time (one launch per step)" if one_launch
+                                            else "CUDA events bracketing the kernel in a second graph replay"),
+                     "event_bracketed_launch_ms": k_ms,
+                     "traffic_source": "ncu dram__bytes_read+write per launch recorded in profiles/ncu_traffic.txt"},
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }
 
     if not args.no_c1 and args.batch == 1:
-        line["c1_w8_decode_b1"] = run_c1(gen, dev, 48 * 500, 48)
+        line["c1_w8_decode_b1"] = run_c1(gen, dev, 48 * 500, 48,
+                                         cpu_seconds=0.0 if (args.no_cpu_baseline or world > 1) else 5.0)
+
+    if args.m32 and args.batch == 1:
+        line["m32_dense_bmm_b1"] = run_m32_bmm(gen, dev, args.m32, max(args.warmup, 3))
 
     if args.trace and fused and args.batch == 1:
         line["phase_timeline_us"] = trace_phases(layers, x, logits, outs, clk.summary().get("sm_mhz") or 1965.0)
@@ -586,6 +631,17 @@ def main():
         line["e2e"] = {"value": args.e2e_steps * args.batch * world / (e_ms / 1e3), "unit": "tokens/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                        "api": "MoeLayer.forward per step, eager (pinned host buffers)"}
+        if args.batch == 1:
+            hyb = hybrid_layers(lws, dev)
+
+            def hcall(j, xj, lj, oj):
+                oj.copy_(hyb[j](xj, lj))
+            h_ms, _, _ = run_e2e(layers, x, logits, args.e2e_steps, call=hcall)
+            h_ms = max_over_ranks(h_ms)
+            line["e2e"]["hybrid_moe_forward"] = {
+                "value": args.e2e_steps * args.batch * world / (h_ms / 1e3), "unit": "tokens/s",
+                "api": "HybridMoE.forward (all experts offloaded to the cuda backend) per step, pinned host buffers"}
+            del hyb
 
     sweep = {}
     for b in [int(b) for b in args.sweep.split(",") if b]:
@@ -596,10 +652,17 @@ def main():
         s_ms, s_k, _ = run_device(layers, xb_, lb_, ob_, st, 48, profile_layer_class=_lib.K_GATEUP)
         s_ms = max_over_ranks(s_ms)
         byt = sum(d_b[i % L] * (gu_bytes + dn_bytes) for i in range(st))
+        step_gbs = byt / (s_ms / 1e3) / 1e9
         sweep[str(b)] = {"tokens_per_s": st * b * world / (s_ms / 1e3), "ms_per_step": s_ms / st,
                          "expert_weight_gbs": byt * world / (s_ms / 1e3) / 1e9,
                          "gateup_kernel_gbs": statistics.mean(d * gu_bytes for d in d_b) / (s_k / 1e3) / 1e9,
-                         "distinct_experts_mean": statistics.mean(d_b)}
+                         "distinct_experts_mean": statistics.mean(d_b),
+                         "launches_per_step": layers[0].last_launch_count(),
+                         "roofline": {"bound": "hbm", "scope": "whole step (every kernel of the step)",
+                                      "achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
+                                      "peak_source": peak_kind,
+                                      "algorithmic_bytes_per_step": byt / st,
+                                      "traffic": read_traffic("sweep", b)}}
     if sweep:
         line["sweep"] = sweep
 
@@ -655,15 +718,121 @@ def quantized_stack(gen, device, E, n, k, bits, group):
     return q, s
 
 
-def zipf_router_bias(E: int, alpha: float, gen, device):
-    """b_e = log(z_e), z proportional to rank^-alpha over a seeded expert permutation."""
+def zipf_router_bias(E: int, alpha: float, gen, device, beta: float = 1.0):
+    """b_e = beta * log(z_e), z proportional to rank^-alpha over a seeded expert permutation."""
     import torch
 
     perm = torch.randperm(E, generator=gen, device=device)
     ranks = torch.empty(E, device=device)
     ranks[perm] = torch.arange(1, E + 1, device=device, dtype=torch.float32)
     z = ranks ** (-alpha)
-    return torch.log(z / z.sum())
+    return beta * torch.log(z / z.sum())
+
+
+_ZIPF_BETA = {}
+
+
+def calibrate_zipf_beta(E: int, top_k: int, H: int, alpha: float, device, renorm: bool = True, tokens: int = 8192):
+    """The router bias scale beta for which the empirical top-k selection
+    frequency of N(0, 1) tokens through an N(0, 0.02) bf16 router follows
+    Zipf(alpha) over the bias ranks: bisection on beta so that the slope of
+    log(frequency) against log(rank), fitted over the ranks that are selected
+    at all, equals -alpha.  Seeded and cached per (E, k, H, alpha)."""
+    import numpy as np
+    import torch
+
+    key = (E, top_k, H, alpha)
+    if key in _ZIPF_BETA:
+        return _ZIPF_BETA[key]
+    gen = torch.Generator(device=device).manual_seed(4242)
+    x = torch.randn(tokens, H, generator=gen, device=device).to(torch.bfloat16)
+    wr = (torch.randn(E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    base = (x @ wr.T).float()
+    perm = torch.randperm(E, generator=gen, device=device)
+    ranks = torch.empty(E, device=device)
+    ranks[perm] = torch.arange(1, E + 1, device=device, dtype=torch.float32)
+    logz = torch.log(ranks ** (-alpha) / (ranks ** (-alpha)).sum())
+
+    def fitted(beta):
+        lg = (base + beta * logz).to(torch.bfloat16).float()
+        p = torch.softmax(lg, dim=-1).to(torch.bfloat16)
+        ids = torch.topk(p, top_k, dim=-1).indices
+        freq = torch.bincount(ids.reshape(-1), minlength=E).float()
+        f = freq[perm].cpu().numpy()  # by bias rank 1..E
+        r = np.arange(1, E + 1, dtype=np.float64)
+        sel = f > 0
+        return -np.polyfit(np.log(r[sel]), np.log(f[sel]), 1)[0]
+
+    lo, hi = 0.0, 8.0
+    for _ in range(30):
+        mid = 0.5 * (lo + hi)
+        if fitted(mid) < alpha:
+            lo = mid
+        else:
+            hi = mid
+    beta = 0.5 * (lo + hi)
+    _ZIPF_BETA[key] = (beta, float(fitted(beta)))
+    return _ZIPF_BETA[key]
+
+
+def qlin(q, s, e: int, bits: int, group: int):
+    """Expert e of a stacked [E, N, K*bits/8] code / [E, N, SS] scale pair as the
+    oracle's QuantLinear (the host copy of the same device weights)."""
+    import numpy as np
+    import torch
+
+    from oracle import moe_oracle as mo
+
+    words = q[e].contiguous().cpu().numpy().view(np.int32)
+    kdim = words.shape[1] * 32 // bits
+    g = group if group > 0 else kdim
+    sc = s[e, :, :kdim // g].to(torch.float32).cpu().numpy()
+    return mo.QuantLinear(words, sc, g, bits)
+
+
+def prefill_cpu_baseline(name, lw, x, ids, wts, shared, E, k, T, seconds):
+    """The oracle port of the reference CPU path (CPUMoEBackend GPTQ branch and
+    the shared-expert add) on the same weights, routing and tokens.  Mixtral's
+    1.4 TFLOP layer is sampled: the experts are run in ascending order until
+    `seconds` of CPU time, and the time is scaled by the (token, expert) pairs
+    of all experts over those run."""
+    import numpy as np
+    import torch
+
+    from oracle import moe_oracle as mo
+
+    xb = x.view(torch.int16).cpu().numpy().view(np.uint16)
+    ib = ids.cpu().numpy()
+    wb = wts.view(torch.int16).cpu().numpy().view(np.uint16)
+    g = lw.group_size
+    counts = np.bincount(ib.reshape(-1), minlength=E)
+    busy, pairs_done, run = 0.0, 0, []
+    for e in range(E):
+        if counts[e] == 0:
+            continue
+        ex = {e: tuple(qlin(q, s_, e, lw.bits, g) for q, s_ in ((lw.gate_q, lw.gate_s), (lw.up_q, lw.up_s),
+                                                                   (lw.down_q, lw.down_s)))}
+        sel = np.where(ib == e, ib, -1)
+        t0 = time.perf_counter()
+        mo.offload_forward_f32(xb, sel, wb, ex, None) if sel.max() >= 0 else None
+        busy += time.perf_counter() - t0
+        pairs_done += int(counts[e])
+        run.append(e)
+        if busy > seconds:
+            break
+    total = busy * counts.sum() / max(pairs_done, 1)
+    sample = f"experts {run[0]}..{run[-1]} ({len(run)} of {int((counts > 0).sum())} routed, {pairs_done} of " \
+             f"{int(counts.sum())} pairs) timed once, scaled by pairs"
+    if shared is not None:
+        sh = tuple(qlin(shared[a], shared[b], 0, lw.bits, g) for a, b in (("gate_q", "gate_s"), ("up_q", "up_s"),
+                                                                        ("down_q", "down_s")))
+        gv = shared["gate_vec"].view(torch.int16).cpu().numpy().view(np.uint16)
+        t0 = time.perf_counter()
+        mo.shared_expert_f32(xb, gv, sh)
+        total += time.perf_counter() - t0
+        sample += "; shared expert timed once"
+    return {"value": T / total, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+            "sample": f"{name} layer of {T} tokens: {sample}; oracle port of CPUMoEBackend GPTQ path"}
 
 
 def bf16_peak():
@@ -675,7 +844,7 @@ def bf16_peak():
         return 1590.0, "fallback"
 
 
-def run_prefill(name: str, gen, device, steps: int, warmup: int):
+def run_prefill(name: str, gen, device, steps: int, warmup: int, cpu_seconds: float = 0.0):
     """Device time of MoeLayer.forward (route + permute + pack + grouped GEMMs +
     combine, shared expert included) on one prefill batch, CUDA events on the
     launching stream; the expert weights (> L2) are re-read every step."""
@@ -705,8 +874,11 @@ def run_prefill(name: str, gen, device, steps: int, warmup: int):
     x = torch.randn(T, H, generator=gen, device=device).to(torch.bfloat16)
     wr = (torch.randn(E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
     logits = x @ wr.T
+    zipf = None
     if c["zipf"]:
-        logits = (logits.float() + zipf_router_bias(E, c["zipf"], gen, device)).to(torch.bfloat16)
+        beta, fit = calibrate_zipf_beta(E, k, H, c["zipf"], device, renorm=c["renorm"])
+        zipf = {"alpha": c["zipf"], "beta": beta, "fitted_alpha": fit}
+        logits = (logits.float() + zipf_router_bias(E, c["zipf"], gen, device, beta)).to(torch.bfloat16)
     out = torch.empty_like(x)
     for _ in range(max(warmup, 3)):
         layer.forward(x, logits, out=out)
@@ -728,7 +900,7 @@ def run_prefill(name: str, gen, device, steps: int, warmup: int):
     e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    ids, _ = layer.route(logits)
+    ids, wts = layer.route(logits)
     per_expert = torch.bincount(ids.reshape(-1), minlength=E)
     flops_routed = 2.0 * T * k * 3 * H * I
     flops_gateup = 2.0 * T * k * 2 * H * I
@@ -741,18 +913,103 @@ def run_prefill(name: str, gen, device, steps: int, warmup: int):
         "routed_tflops": flops_routed / (ms / 1e3) / 1e12,
         "tokens_per_expert": {"max": int(per_expert.max()), "min": int(per_expert.min()),
                               "mean": float(per_expert.float().mean())},
-        "roofline": {"bound": "tensor", "kernel": f"grouped_gemm_kernel<{bits},gate/up>", "achieved": gu_tf,
-                     "peak": peak, "unit": "TFLOP/s", "frac": gu_tf / peak, "peak_source": peak_kind,
-                     "algorithmic_flops_per_launch": flops_gateup, "avg_launch_ms": kern["gateup"]},
         "down_kernel_tflops": 2.0 * T * k * H * I / (kern["down"] / 1e3) / 1e12,
         "down_avg_launch_ms": kern["down"],
     }
+    gemm_roof = {"bound": "tensor", "kernel": f"grouped_gemm_kernel<{bits},gate/up>", "achieved": gu_tf,
+                 "peak": peak, "unit": "TFLOP/s", "frac": gu_tf / peak, "peak_source": peak_kind,
+                 "algorithmic_flops_per_launch": flops_gateup, "avg_launch_ms": kern["gateup"],
+                 "kernel_time_source": "CUDA events bracketing the kernel (eager launches)"}
+    if name == "qwen2":
+        # about 124 FLOP per weight byte: below the ridge, so the bound is HBM: the
+        # distinct routed experts' codes + scales plus the shared expert, once per step
+        def proj_bytes(q):
+            kdim = q.shape[2] * 8 // bits
+            return q[0].numel() + q.shape[1] * (kdim // (grp if grp > 0 else kdim)) * 2  # codes + bf16 scales
+
+        per_e = proj_bytes(gq) + proj_bytes(uq) + proj_bytes(dq)
+        distinct = int((per_expert > 0).sum())
+        sh_bytes = sum(proj_bytes(shared[a]) for a in ("gate_q", "up_q", "down_q"))
+        step_bytes = distinct * per_e + sh_bytes
+        gbs = step_bytes / (ms / 1e3) / 1e9
+        hpeak, hkind = hbm_peak()
+        res["roofline"] = {"bound": "hbm", "scope": "whole step", "achieved": gbs, "peak": hpeak, "unit": "GB/s",
+                           "frac": gbs / hpeak, "peak_source": hkind, "algorithmic_bytes_per_step": step_bytes,
+                           "distinct_routed_experts": distinct, "shared_expert_bytes": sh_bytes}
+        res["gateup_gemm_tensor_roofline"] = gemm_roof
+        res["zipf"] = zipf
+    else:
+        res["roofline"] = gemm_roof
+    if cpu_seconds > 0:
+        res["cpu_baseline"] = prefill_cpu_baseline(name, lw, x, ids, wts, shared, E, k, T, cpu_seconds)
     del layer, lw, gq, gs, uq, us, dq, ds
     torch.cuda.empty_cache()
     return res
 
 
-def run_c1(gen, device, steps: int, warmup: int, n_layers: int = 6):
+def run_m32_bmm(gen, device, steps: int, warmup: int, n_layers: int = 4):
+    """The reference's GPU-resident batch-1 comparator (the fused stacked-bmm
+    decode of hybrid_moe.py:3442-3500) restated in PyTorch on dense bf16
+    Qwen3-shaped experts: unique routed ids read to the host, the routed
+    experts' gate/up/down stacked, three bmm + SiLU * up, and the weighted sum
+    over the routed experts.  n_layers distinct layers (1.2 GB of bf16 experts
+    each) are cycled so every step reads its experts from HBM.  CUDA events
+    around `steps` steps; the block's host reads are inside the timed region,
+    as they are in the reference."""
+    import torch
+    import torch.nn.functional as F
+
+    E, H, I, k = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["top_k"]
+    w1 = [(torch.randn(E, I, H, generator=gen, device=device) * 0.02).to(torch.bfloat16) for _ in range(n_layers)]
+    w3 = [(torch.randn(E, I, H, generator=gen, device=device) * 0.02).to(torch.bfloat16) for _ in range(n_layers)]
+    w2 = [(torch.randn(E, H, I, generator=gen, device=device) * 0.02).to(torch.bfloat16) for _ in range(n_layers)]
+    xs = [torch.randn(1, H, generator=gen, device=device).to(torch.bfloat16) for _ in range(n_layers)]
+    wr = [(torch.randn(E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16) for _ in range(n_layers)]
+    route = []
+    for x, r in zip(xs, wr):
+        p = torch.softmax((x @ r.T).float(), dim=-1)
+        w, ids = torch.topk(p, k, dim=-1)
+        route.append((ids, (w / w.sum(dim=-1, keepdim=True)).to(torch.bfloat16)))
+    gpu_mask = torch.ones(E, dtype=torch.bool, device=device)
+    outs = [torch.zeros(1, H, dtype=torch.bfloat16, device=device) for _ in range(n_layers)]
+
+    def block(j):
+        ids, w = route[j]
+        unique_routed = torch.unique(ids).cpu().tolist()
+        mask = gpu_mask.cpu().tolist()
+        routed = [e for e in unique_routed if mask[e]]
+        g1 = torch.stack([w1[j][e] for e in routed])
+        g3 = torch.stack([w3[j][e] for e in routed])
+        g2 = torch.stack([w2[j][e] for e in routed])
+        xb = xs[j].expand(len(routed), -1).unsqueeze(1)
+        h = F.silu(torch.bmm(xb, g1.transpose(1, 2))) * torch.bmm(xb, g3.transpose(1, 2))
+        o = torch.bmm(h, g2.transpose(1, 2)).squeeze(1)
+        rt = torch.tensor(routed, device=device, dtype=torch.long)
+        match = (rt.unsqueeze(1) == ids[0].unsqueeze(0)).to(w.dtype)
+        outs[j][0] = (o * (match * w[0].unsqueeze(0)).sum(dim=1).unsqueeze(1)).sum(dim=0)
+
+    for i in range(warmup):
+        block(i % n_layers)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        block(i % n_layers)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    per_step = k * 3 * H * I * 2  # the routed experts' bf16 weights
+    peak, peak_kind = hbm_peak()
+    gbs = per_step / (ms / 1e3) / 1e9
+    del w1, w2, w3
+    torch.cuda.empty_cache()
+    return {"ms_per_step": ms, "tokens_per_s": 1e3 / ms, "expert_weight_gbs": gbs, "frac_of_hbm_peak": gbs / peak,
+            "peak_source": peak_kind, "algorithmic_bytes_per_step": per_step, "steps": steps,
+            "weights": "dense bf16, 8 routed experts of E=128 H=2048 I=768", "layers_cycled": n_layers,
+            "note": "stacks copy the routed weights each step (reads + writes 2x the algorithmic bytes)"}
+
+
+def run_c1(gen, device, steps: int, warmup: int, n_layers: int = 6, cpu_seconds: float = 0.0):
     """Config 1: Qwen3-shaped W8 per-output-channel decode at batch 1 (the
     single-launch multi-token kernel; the single-token kernel is W4 only).
     n_layers distinct layers (0.6 GB of expert weights each) are cycled in a
@@ -764,33 +1021,46 @@ def run_c1(gen, device, steps: int, warmup: int, n_layers: int = 6):
     from nano_ktrans_b200.weights import LayerWeights
 
     E, H, I, k = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["top_k"]
-    layers, x, logits = [], [], []
+    layers, x, logits, lws = [], [], [], []
     for _ in range(n_layers):
         gq, gs = quantized_stack(gen, device, E, I, H, 8, 0)
         uq, us = quantized_stack(gen, device, E, I, H, 8, 0)
         dq, ds = quantized_stack(gen, device, E, H, I, 8, 0)
         lw = LayerWeights(bits=8, group_size=0, gate_q=gq, gate_s=gs, up_q=uq, up_s=us, down_q=dq, down_s=ds)
         layers.append(MoeLayer(lw, top_k=k, router_use_softmax=True, normalize_topk_prob=True, max_tokens=1))
+        lws.append(lw)
         xi = torch.randn(1, H, generator=gen, device=device).to(torch.bfloat16)
         wr = (torch.randn(E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
         x.append(xi)
         logits.append(xi @ wr.T)
     outs = [torch.empty_like(xi) for xi in x]
     ms, k_ms, launches = run_device(layers, x, logits, outs, steps, warmup, profile_layer_class=_lib.K_DECODE_FUSED)
+    ev_ms = k_ms
+    if launches == 1:
+        k_ms = ms / steps  # one launch per step: the graph-replay step time is the kernel time
     per_expert = 3 * H * I + (2 * I + H) * 2  # int8 codes + one bf16 scale per output row: 4,725,760 B
     distinct = [int(torch.unique(lay.route(lg)[0]).numel()) for lay, lg in zip(layers, logits)]
     step_bytes = sum(distinct[i % n_layers] for i in range(steps)) / steps * per_expert
     peak, peak_kind = hbm_peak()
     gbs = step_bytes / (ms / steps / 1e3) / 1e9
     kgbs = step_bytes / (k_ms / 1e3) / 1e9
+    cpu = None
+    if cpu_seconds > 0:
+        rate, n, busy = cpu_reference_rate(lws, torch.stack(x), torch.stack(logits), cpu_seconds, 10 ** 6)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+               "sample": f"{n} layer-steps at batch 1 ({busy:.1f} s), oracle port of CPUMoEBackend GPTQ path "
+                         "(W8 per-channel) on the same weights"}
     del layers
     torch.cuda.empty_cache()
-    return {"config": "C1: E=128 H=2048 I=768 top8 renormalised, W8 per-channel, bf16 scales, batch 1",
+    return {"cpu_baseline": cpu,
+            "config": "C1: E=128 H=2048 I=768 top8 renormalised, W8 per-channel, bf16 scales, batch 1",
             "tokens_per_s": steps / (ms / 1e3), "ms_per_step": ms / steps, "launches_per_step": launches,
             "expert_weight_gbs": gbs, "expert_weight_frac_of_peak": gbs / peak,
             "roofline": {"bound": "hbm", "kernel": "moe_decode_fused_kernel<8>", "achieved": kgbs, "peak": peak,
                          "unit": "GB/s", "frac": kgbs / peak, "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": step_bytes, "avg_launch_ms": k_ms,
+                         "kernel_time_source": "graph-replay step time (one launch per step)" if launches == 1
+                         else "CUDA events bracketing the kernel", "event_bracketed_launch_ms": ev_ms,
                          "traffic": read_traffic("decode_fused_w8", 1)},
             "layers_cycled": n_layers}
 
@@ -802,7 +1072,8 @@ def prefill_block(args, dev, rank):
     out = {}
     for name in [n for n in args.prefill.split(",") if n]:
         gen = torch.Generator(device=dev).manual_seed(args.seed + 17 + 1000 * rank)
-        r = run_prefill(name, gen, dev, args.prefill_steps, args.warmup)
+        r = run_prefill(name, gen, dev, args.prefill_steps, args.warmup,
+                        0.0 if (args.no_cpu_baseline or rank != 0) else args.cpu_seconds)
         ms = max_over_ranks(r["ms_per_step"])
         world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
         r["ms_per_step"] = ms
@@ -834,7 +1105,8 @@ def run_ep(args, world, rank, dev, uniq, lws):
     L = len(lws)
     gen = torch.Generator(device=dev).manual_seed(args.seed + 5000)  # same router and bias on every rank
     routers = [(torch.randn(E, H, generator=gen, device=dev) * 0.02).to(torch.bfloat16) for _ in range(L)]
-    biases = [zipf_router_bias(E, 1.2, gen, dev) for _ in range(L)]
+    beta, fit_alpha = calibrate_zipf_beta(E, k, H, 1.2, dev, renorm=True)
+    biases = [zipf_router_bias(E, 1.2, gen, dev, beta) for _ in range(L)]
     tgen = torch.Generator(device=dev).manual_seed(args.seed + 6000 + rank)  # this rank's tokens
 
     def batch(n_global):
@@ -846,7 +1118,7 @@ def run_ep(args, world, rank, dev, uniq, lws):
     tp, xp, lp = batch(n_prefill)
     td, xd, ld = batch(n_decode)
     res = {"placement": "frequency-balanced (prefill batch routing counts, all ranks)", "world": world,
-           "zipf_alpha": 1.2, "zipf_beta": 1.0}
+           "zipf": {"alpha": 1.2, "beta": beta, "fitted_alpha": fit_alpha}}
 
     if world == 1:
         layers = [MoeLayer(lw, top_k=k, router_use_softmax=True, normalize_topk_prob=True, max_tokens=tp)
@@ -903,10 +1175,74 @@ def run_ep(args, world, rank, dev, uniq, lws):
                       "routed_tflops": flops_layer * L / (ms / 1e3) / 1e12}
     ms = timed(xd, ld, 3 * args.ep_steps)
     res["decode"] = {"global_tokens": n_decode, "ms_per_48_layers": ms, "tokens_per_s": n_decode / (ms / 1e3)}
+    res["ep_parity"] = ep_parity(layers, uniq, xp, lp, xd, ld, world, rank, tp)
+    if world == 1 and not args.no_cpu_baseline and args.cpu_seconds > 0:
+        res["cpu_baseline"] = ep_cpu_baseline(layers[0], lws[0], xp[0], lp[0], xd[0], ld[0], L, args.cpu_seconds)
     for lay in layers:
         lay.close()
     torch.cuda.empty_cache()
     return res
+
+
+def ep_cpu_baseline(layer, lw, xp, lp, xd, ld, n_layers, seconds):
+    """The oracle port of the reference CPU path on one layer of the stack
+    (the prefill batch sampled by experts, the decode batch by whole steps),
+    stated per pass over all n_layers layers (one layer x n_layers)."""
+    import torch
+
+    E, k = CFG["experts"], CFG["top_k"]
+    ids, w = layer.route(lp)
+    pre = prefill_cpu_baseline("c5-layer0", lw, xp, ids, w, None, E, k, xp.shape[0], seconds / 2)
+    rate, n, busy = cpu_reference_rate([lw], xd[None], ld[None], seconds / 2, 10 ** 6)
+    return {"prefill": {"value": pre["value"] / n_layers, "unit": "tokens/s", "cores": pre["cores"], "kind": "port",
+                        "sample": pre["sample"] + f"; one layer x {n_layers}"},
+            "decode": {"value": rate / n_layers, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+                       "sample": f"{n} steps of layer 0 at {xd.shape[0]} tokens ({busy:.1f} s); one layer x "
+                                 f"{n_layers}; oracle port of CPUMoEBackend GPTQ path"}}
+
+
+def ep_parity(layers, uniq, xp, lp, xd, ld, world, rank, max_tokens, n_check: int = 2):
+    """Bit-compare the expert-parallel output of this rank's tokens with the
+    single-GPU MoeLayer.forward of the same tokens on this rank's GPU, for the
+    prefill and decode batches of the first n_check layers; the mismatch
+    counts are summed over ranks.  At one rank the expert-parallel layer runs
+    with a loopback exchange."""
+    import torch
+
+    from nano_ktrans_b200.expert_parallel import (EpMoeLayer, LoopbackComm, TorchDistComm, plan_placement,
+                                                  shard_layer)
+    from nano_ktrans_b200.moe_layer import MoeLayer
+
+    E, k = CFG["experts"], CFG["top_k"]
+    own = []
+    if world == 1:
+        comm = LoopbackComm()
+        slot = plan_placement(E, 1)
+        ep = [EpMoeLayer(shard_layer(uniq[i % len(uniq)], slot, 0, 1), num_experts=E, top_k=k,
+                         slot_of_expert=slot, rank=0, world=1, max_tokens=max_tokens) for i in range(n_check)]
+        own = ep
+    else:
+        comm = TorchDistComm()
+        ep = layers[:n_check]
+    tokens = torch.zeros(2, dtype=torch.float64, device=xp[0].device)  # checked tokens, mismatching tokens
+    for i in range(n_check):
+        ref = MoeLayer(uniq[i % len(uniq)], top_k=k, router_use_softmax=True, normalize_topk_prob=True,
+                       max_tokens=max_tokens)
+        for xs, lg in ((xp, lp), (xd, ld)):
+            got = ep[i].forward(xs[i], lg[i], comm)[0].clone()
+            want = ref.forward(xs[i], lg[i]).clone()
+            bad = (got.view(torch.int16) != want.view(torch.int16)).any(dim=1)
+            tokens[0] += got.shape[0]
+            tokens[1] += bad.sum()
+        torch.cuda.synchronize()
+        ref.close()
+    for lay in own:
+        lay.close()
+    if torch.distributed.is_initialized():
+        torch.distributed.all_reduce(tokens)
+    return {"checked_tokens": int(tokens[0]), "mismatches": int(tokens[1]), "layers": n_check,
+            "batches": "prefill and decode", "compare": "bf16 bit pattern vs MoeLayer.forward on the same GPU",
+            "ranks": world}
 
 
 def read_traffic(kernel: str, batch: int):
