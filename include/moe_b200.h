@@ -17,6 +17,11 @@
  *                        index_add_ combine cpu_moe.py:528-538)
  *   moe_forward          HybridMoE.forward with every expert offloaded
  *                        (hybrid_moe.py:3310-3570): route + experts
+ *   moe_router_logits    the router projection `self.gate(hidden_states)`
+ *                        nano_ktrans/models/mixtral.py:127, :212 (bf16
+ *                        nn.Linear, no bias)
+ *   moe_forward_x        router projection + moe_forward: the MoE block of
+ *                        models/mixtral.py:212-218 from hidden states
  *   moe_dequant_rows     GPTQLinearWeight.dequantize
  *                        nano_ktrans/kernels/weight_loader.py:57-69, for the
  *                        bit-exact dequantization check
@@ -134,6 +139,19 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
                 int32_t num_tokens, uint16_t* out_dev, int64_t* topk_ids_dev,
                 uint16_t* topk_weights_dev, void* stream);
 
+/* Router logits [T, E] bf16 = bf16(x [T, H] . router_w [E, H]^T), fp32
+ * accumulation (the reference's bf16 nn.Linear gate).  x_dev and
+ * router_w_dev 16-byte aligned; hidden_size a multiple of 32. */
+int moe_router_logits(void* handle, const uint16_t* x_dev, const uint16_t* router_w_dev,
+                      int32_t num_tokens, uint16_t* logits_dev, void* stream);
+
+/* moe_router_logits followed by moe_forward.  logits_dev (may be NULL: the
+ * handle's workspace is used) receives the logits, as the reference's MoE
+ * block also returns them.  topk_ids_dev / topk_weights_dev may be NULL. */
+int moe_forward_x(void* handle, const uint16_t* x_dev, const uint16_t* router_w_dev,
+                  int32_t num_tokens, uint16_t* out_dev, int64_t* topk_ids_dev,
+                  uint16_t* topk_weights_dev, uint16_t* logits_dev, void* stream);
+
 /* ---- Expert parallelism (no counterpart in the reference, whose offload
  * backends are single-device) ----
  * The routed experts are split over `world` ranks; expert e lives on rank
@@ -213,7 +231,13 @@ enum moe_option {
   /* Token-tile width of the grouped GEMM: 0 (default) = the smallest of
    * 16/32/64/128 covering the mean tokens per routed expert; or one of those
    * four values. */
-  MOE_OPT_GEMM_TILE = 4
+  MOE_OPT_GEMM_TILE = 4,
+  /* Expert projections of batches the single-launch kernels and the GEMM do
+   * not take: 1 (default) = weight-streaming tensor-core kernels (each active
+   * expert's rows read once per call, applied to up to 8 of its tokens at a
+   * time) when the layer is W4 with inter, hidden and group_size multiples of
+   * 128; 0 = the CUDA-core matvec kernels. */
+  MOE_OPT_STREAM = 5
 };
 
 /* Copy the phase stamps of the last traced single-launch decode step, 16 per

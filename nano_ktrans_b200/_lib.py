@@ -15,7 +15,7 @@ HEADER_PATH = os.path.join(os.path.dirname(PKG_DIR), "include", "moe_b200.h")
 
 MOE_OK, MOE_EINVAL, MOE_ECUDA, MOE_ENOWEIGHTS, MOE_ERANGE, MOE_EDEVICE = range(6)
 K_ROUTE, K_PERMUTE, K_GATEUP, K_DOWN, K_COMBINE, K_DECODE_FUSED = range(1, 7)
-OPT_DECODE_FUSED, OPT_TRACE, OPT_GEMM, OPT_GEMM_TILE = 1, 2, 3, 4
+OPT_DECODE_FUSED, OPT_TRACE, OPT_GEMM, OPT_GEMM_TILE, OPT_STREAM = 1, 2, 3, 4, 5
 
 _DESC_FIELDS = ("num_experts", "top_k", "hidden_size", "inter_size", "bits", "group_size",
                 "router_use_softmax", "normalize_topk_prob", "max_tokens", "shared_inter")
@@ -50,6 +50,8 @@ SIGNATURES = {
     "moe_route": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "moe_experts_forward": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp]),
     "moe_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "moe_router_logits": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "moe_forward_x": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
     "moe_dequant_rows": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp]),
     "moe_read_status": (_i32, [_vp, ctypes.POINTER(_i32), _vp]),
     "moe_last_launch_count": (_i32, [_vp]),

@@ -37,6 +37,7 @@ struct Handle {
   float* sh_h = nullptr;   // [max_tokens][I_s]
   float* sh_y = nullptr;   // [max_tokens][H]
   float* sh_g = nullptr;   // [max_tokens]
+  uint16_t* logits_tmp = nullptr;  // [max_tokens][E] router logits of moe_forward_x
   int64_t* ids_tmp = nullptr;
   uint16_t* w_tmp = nullptr;
   unsigned long long* grid_bar = nullptr;  // grid-barrier arrival counter of the fused decode kernel
@@ -46,6 +47,7 @@ struct Handle {
   int32_t* tile_off = nullptr;  // [E+1]
   int gemm_mode = 1;            // 0 never, 1 by batch size, 2 whenever the shape allows
   int gemm_tile = 0;            // token-tile width of the GEMM launches: 0 by batch, else 16/32/64/128
+  int stream_mode = 1;          // 1: weight-streaming kernels where eligible, 0: matvec kernels
   bool gemm_maps = false;       // tensor maps encoded (shape supported, driver entry point found)
   // activation maps, one per token-tile width 16 << i
   alignas(64) unsigned char tm_x[moe::kGemmTileWidths][128];  // fp16 [max_pairs][H] over ybuf (x in pair order)
@@ -237,7 +239,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
                o_nact = take(4), o_sorted = take(4 * P), o_pos = take(4 * P), o_h = take(4 * P * I),
                o_y = take(4 * P * H), o_shh = take(S ? 4 * T * S : 0), o_shy = take(S ? 4 * T * H : 0),
                o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P), o_bar = take(8),
-               o_tiles = take(4 * (E + 1)), o_shtab = take(4 * 8), o_gids = take(8 * P);
+               o_tiles = take(4 * (E + 1)), o_shtab = take(4 * 8), o_gids = take(8 * P), o_lg = take(2 * T * E);
   h->ws_bytes = off;
   cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
   if (e != cudaSuccess) {
@@ -266,6 +268,7 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   h->tile_off = reinterpret_cast<int32_t*>(b + o_tiles);
   h->sh_tables = reinterpret_cast<int32_t*>(b + o_shtab);
   h->slot_ids = reinterpret_cast<int64_t*>(b + o_gids);
+  h->logits_tmp = reinterpret_cast<uint16_t*>(b + o_lg);
   e = cudaMemset(h->ws, 0, h->ws_bytes);
   if (e != cudaSuccess) {
     fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
@@ -464,6 +467,16 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     prof_mark(h, MOE_K_DOWN, true, st);
     if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (down): shared-memory opt-in refused");
     launches += 2;
+  } else if (h->stream_mode && moe::stream_eligible(d.bits, gate, up, down, max_active)) {
+    prof_mark(h, MOE_K_GATEUP, false, st);
+    int rc = moe::launch_stream_gateup(x, h->rt, k, max_active, gate, up, h->hbuf, h->rt.status, h->num_sms, st);
+    prof_mark(h, MOE_K_GATEUP, true, st);
+    if (rc < 0) return fail(h, MOE_ECUDA, "streaming gate/up: launch refused");
+    prof_mark(h, MOE_K_DOWN, false, st);
+    rc = moe::launch_stream_down(h->hbuf, h->rt, max_active, down, h->ybuf, h->rt.status, h->num_sms, st);
+    prof_mark(h, MOE_K_DOWN, true, st);
+    if (rc < 0) return fail(h, MOE_ECUDA, "streaming down: launch refused");
+    launches += 2;
   } else {
     prof_mark(h, MOE_K_GATEUP, false, st);
     launches += moe::launch_gateup(d.bits, x, h->rt, k, max_active, T, 0, gate, up, h->hbuf, h->num_sms, st);
@@ -567,6 +580,37 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
                     h->d.normalize_topk_prob != 0, ids, wts, st);
   prof_mark(h, MOE_K_ROUTE, true, st);
   return experts_forward(h, x_dev, ids, wts, T, nullptr, true, out_dev, st, 1);
+}
+
+int moe_router_logits(void* handle, const uint16_t* x_dev, const uint16_t* router_w_dev, int32_t T,
+                      uint16_t* logits_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (T < 0) return fail(h, MOE_EINVAL, "moe_router_logits: negative token count");
+  if (T == 0) return MOE_OK;
+  if (x_dev == nullptr || router_w_dev == nullptr || logits_dev == nullptr)
+    return fail(h, MOE_EINVAL, "moe_router_logits: null device pointer");
+  if (!moe::router_shape_ok(h->d.num_experts, h->d.hidden_size, x_dev, router_w_dev))
+    return fail(h, MOE_EINVAL, "moe_router_logits: x and the router weight must be 16-byte aligned");
+  moe::launch_router_logits(x_dev, router_w_dev, T, h->d.num_experts, h->d.hidden_size, logits_dev,
+                            static_cast<cudaStream_t>(stream));
+  return check_launch(h, "moe_router_logits");
+}
+
+int moe_forward_x(void* handle, const uint16_t* x_dev, const uint16_t* router_w_dev, int32_t T, uint16_t* out_dev,
+                  int64_t* ids_dev, uint16_t* w_dev, uint16_t* logits_dev, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (int rc = check_forward_args(h, x_dev, out_dev, T)) return rc;
+  if (T == 0) {
+    h->last_launches = 0;
+    return MOE_OK;
+  }
+  uint16_t* lg = logits_dev ? logits_dev : h->logits_tmp;
+  if (int rc = moe_router_logits(handle, x_dev, router_w_dev, T, lg, stream)) return rc;
+  if (int rc = moe_forward(handle, x_dev, lg, T, out_dev, ids_dev, w_dev, stream)) return rc;
+  h->last_launches += 1;
+  return MOE_OK;
 }
 
 int moe_ep_dispatch(void* handle, const uint16_t* x_dev, const int64_t* ids_dev, int32_t T,
@@ -693,6 +737,10 @@ int moe_set_option(void* handle, int32_t option, int32_t value) {
       if (value != 0 && value != 16 && value != 32 && value != 64 && value != 128)
         return fail(h, MOE_EINVAL, "moe_set_option(gemm tile): value must be 0, 16, 32, 64 or 128");
       h->gemm_tile = value;
+      return MOE_OK;
+    case MOE_OPT_STREAM:
+      if (value < 0 || value > 1) return fail(h, MOE_EINVAL, "moe_set_option(stream): value must be 0 or 1");
+      h->stream_mode = value;
       return MOE_OK;
     case MOE_OPT_TRACE:
       if (value && h->trace == nullptr) {

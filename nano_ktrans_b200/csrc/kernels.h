@@ -30,6 +30,12 @@ struct QuantProj {
 void launch_route(const uint16_t* logits, int T, int E, int top_k, bool use_softmax, bool renorm,
                   int64_t* ids, uint16_t* weights, cudaStream_t st);
 
+// logits[t][e] = bf16(sum_h x[t][h] * wr[e][h]), fp32 accumulation; x [T][H]
+// and wr [E][H] bf16, 16-byte aligned, H a multiple of 32.
+bool router_shape_ok(int E, int H, const void* x, const void* wr);
+void launch_router_logits(const uint16_t* x, const uint16_t* wr, int T, int E, int H, uint16_t* logits,
+                          cudaStream_t st);
+
 void launch_permute(const int64_t* ids, int T, int top_k, int E, const uint8_t* offload_mask,
                     const RouteTables& rt, cudaStream_t st);
 
@@ -44,6 +50,17 @@ int launch_gateup(int bits, const uint16_t* x, const RouteTables& rt, int top_k,
 // down projection: y[s][n] = down_e(h[s]).
 int launch_down(int bits, const float* h, const RouteTables& rt, int max_active, int num_tokens, int identity_tokens,
                 const QuantProj& down, float* y, int num_sms, cudaStream_t st);
+
+// Weight-streaming tensor-core projections (stream.cu) for batches that give
+// each active expert a few tokens: same inputs and outputs as launch_gateup /
+// launch_down over the routing tables.  W4 with group sizes that are multiples
+// of 128; stream_eligible says whether this layer's shapes fit.  Launchers
+// return 1 when launched, negative when not.
+bool stream_eligible(int bits, const QuantProj& gate, const QuantProj& up, const QuantProj& down, int max_active);
+int launch_stream_gateup(const uint16_t* x, const RouteTables& rt, int top_k, int max_active, const QuantProj& gate,
+                         const QuantProj& up, float* h, int* status, int num_sms, cudaStream_t st);
+int launch_stream_down(const float* h, const RouteTables& rt, int max_active, const QuantProj& down, float* y,
+                       int* status, int num_sms, cudaStream_t st);
 
 // out[t][n] = bf16( sum_{slots by expert asc} w * y[pos] + sg[t] * ys[t][n] )
 void launch_combine(const int64_t* ids, const uint16_t* weights, const RouteTables& rt, int T, int top_k,

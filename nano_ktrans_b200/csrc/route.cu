@@ -52,6 +52,85 @@ void launch_route(const uint16_t* logits, int T, int E, int top_k, bool use_soft
 }
 
 // ---------------------------------------------------------------------------
+// K0: router logits = bf16(x . Wr^T), the reference's `self.gate(hidden)`
+// (nano_ktrans/models/mixtral.py:127, :212: nn.Linear(H, E, bias=False) in
+// bf16, fp32 accumulation, one bf16 rounding).
+//
+// Warp-level tensor-core GEMM: a CTA owns 16 tokens x 8 experts (one
+// m16n8k16 output tile, tokens = M, experts = N) and its 8 warps split K in
+// 32-wide blocks (block b to warp b % 8); the 8 partial tiles are added in
+// warp order in shared memory.  Lane (g, t) takes the 8 consecutive k of
+// block b starting at 8t, from token rows g and g + 8 (A) and expert row g
+// (B); the two mma steps of the block use pairs (0,1),(2,3) and (4,5),(6,7) of
+// those 8 values, the same permutation of K on both operands.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                            const uint16_t* __restrict__ wr, int T, int E, int H,
+                                                            uint16_t* __restrict__ logits) {
+  __shared__ float part[8][16][9];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int tok0 = blockIdx.y * 16, e0 = blockIdx.x * 8;
+  const bool ok_a = tok0 + g < T, ok_b = tok0 + g + 8 < T, ok_w = e0 + g < E;
+  const uint16_t* xa = x + static_cast<size_t>(ok_a ? tok0 + g : 0) * H + 8 * t;
+  const uint16_t* xb = x + static_cast<size_t>(ok_b ? tok0 + g + 8 : 0) * H + 8 * t;
+  const uint16_t* wp = wr + static_cast<size_t>(ok_w ? e0 + g : 0) * H + 8 * t;
+  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+  const int nb = H / 32;
+#pragma unroll 4
+  for (int b = warp; b < nb; b += 8) {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    const uint4 va = ok_a ? *reinterpret_cast<const uint4*>(xa + 32 * b) : z;
+    const uint4 vb = ok_b ? *reinterpret_cast<const uint4*>(xb + 32 * b) : z;
+    const uint4 vw = ok_w ? *reinterpret_cast<const uint4*>(wp + 32 * b) : z;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c0[0]), "+f"(c0[1]), "+f"(c0[2]), "+f"(c0[3])
+        : "r"(va.x), "r"(vb.x), "r"(va.y), "r"(vb.y), "r"(vw.x), "r"(vw.y));
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c1[0]), "+f"(c1[1]), "+f"(c1[2]), "+f"(c1[3])
+        : "r"(va.z), "r"(vb.z), "r"(va.w), "r"(vb.w), "r"(vw.z), "r"(vw.w));
+  }
+  // c[0] = (token g, expert 2t), c[1] = (g, 2t+1), c[2] = (g+8, 2t), c[3] = (g+8, 2t+1)
+  part[warp][g][2 * t] = c0[0] + c1[0];
+  part[warp][g][2 * t + 1] = c0[1] + c1[1];
+  part[warp][g + 8][2 * t] = c0[2] + c1[2];
+  part[warp][g + 8][2 * t + 1] = c0[3] + c1[3];
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int r = threadIdx.x >> 3, c = threadIdx.x & 7;
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) v += part[w][r][c];
+    if (tok0 + r < T && e0 + c < E) logits[static_cast<size_t>(tok0 + r) * E + e0 + c] = f32_to_bf16(v);
+  }
+}
+
+bool router_shape_ok(int E, int H, const void* x, const void* wr) {
+  return E >= 1 && H >= 32 && H % 32 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(wr) % 16 == 0;
+}
+
+void launch_router_logits(const uint16_t* x, const uint16_t* wr, int T, int E, int H, uint16_t* logits,
+                          cudaStream_t st) {
+  if (T <= 0) return;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((E + 7) / 8, (T + 15) / 16);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, router_logits_kernel, x, wr, T, E, H, logits);
+}
+
+// ---------------------------------------------------------------------------
 // K1b: stable counting sort of (token, slot) pairs by expert.  One CTA of
 // 1024 threads.  Shared memory: cnt[E], run[E], off[E+1], warp_sums[32],
 // wcnt[32][E].

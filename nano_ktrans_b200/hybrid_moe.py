@@ -5,10 +5,17 @@ router_logits)`` contract (nano_ktrans/layers/hybrid_moe.py:54-290,
 :3310-3570).  Routing semantics are the reference's (:3321-3329), computed by
 the router kernel; the offloaded experts go through the backend's
 ``submit_forward`` / ``sync_forward`` (:3373-3378, :3563-3567); experts marked
-GPU-resident in ``gpu_experts_mask`` stay dense ``nn.Module``s and are run as
-the reference's per-expert loop does (:3501-3533); the two parts are summed
-(:3570).  When every expert is offloaded, route + experts run as one
-``moe_forward`` call.
+GPU-resident in ``gpu_experts_mask`` are served one of two ways, chosen by
+``resident_experts``:
+
+* ``"kernels"`` (default): by the same kernels, from the backend's quantized
+  weights of every expert (the backend holds all of them), so route + all
+  routed experts + combine are one ``moe_forward`` launch set with no host
+  synchronisation — the resident/offloaded split then only decides who owns
+  the weights, not how the output is computed;
+* ``"modules"``: as dense ``nn.Module``s in the reference's per-expert loop
+  (:3501-3533, with its host reads of the routed ids), summed with the
+  backend's part (:3570) — bit-for-bit the reference's split semantics.
 
 The reference's residency machinery (migration queues, prefetch caches,
 schedulers; hybrid_moe.py:109-254, :2841-3300) is not part of this path; its
@@ -49,6 +56,7 @@ class HybridMoE(nn.Module):
         expert_proj_names: Optional[Dict[str, str]] = None,
         experts_are_packed: bool = False,
         hidden_act: str = "silu",
+        resident_experts: str = "kernels",
         **_residency_kwargs,
     ):
         super().__init__()
@@ -62,11 +70,14 @@ class HybridMoE(nn.Module):
         self.normalize_topk_prob = normalize_topk_prob
         self.experts_are_packed = experts_are_packed
         self.hidden_act = hidden_act
+        if resident_experts not in ("kernels", "modules"):
+            raise ValueError("resident_experts must be 'kernels' or 'modules'")
+        self.resident_experts = resident_experts
         self.has_cpu_experts = bool((~gpu_experts_mask.bool()).any().item())
         self.offload_backend_name = normalize_offload_backend_name(offload_backend)
         if self.offload_backend_name != "cuda":
             raise NotImplementedError(f"this package provides the 'cuda' backend, not '{self.offload_backend_name}'")
-        if not self.has_cpu_experts:
+        if not self.has_cpu_experts and resident_experts == "modules":
             raise ValueError("every expert is GPU-resident: there is no routed-expert work for the cuda backend")
         kwargs = dict(layer_idx=layer_idx, num_experts=num_experts, top_k=top_k, hidden_size=hidden_size,
                       intermediate_size=moe_intermediate_size, gpu_experts_mask=gpu_experts_mask,
@@ -81,7 +92,7 @@ class HybridMoE(nn.Module):
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         layer = self.offload_backend.layer
-        if not bool(self.gpu_experts_mask.bool().any()):
+        if self.resident_experts == "kernels" or not bool(self.gpu_experts_mask.bool().any()):
             t = hidden_states.shape[0]
             ids = torch.empty(t, self.top_k, dtype=torch.int64, device=hidden_states.device)
             w = torch.empty(t, self.top_k, dtype=torch.bfloat16, device=hidden_states.device)

@@ -169,6 +169,47 @@ class MoeLayer:
                                           _ptr(out_weights), _stream_handle(stream)), self._h, "moe_forward")
         return out
 
+    def _check_router(self, router_weight: torch.Tensor) -> None:
+        if (not self._on_device(router_weight) or router_weight.dtype != torch.bfloat16
+                or tuple(router_weight.shape) != (self.num_experts, self.hidden_size)
+                or not router_weight.is_contiguous()):
+            raise ValueError(f"router weight must be a contiguous bf16 [{self.num_experts}, {self.hidden_size}] "
+                             f"tensor on {self.device}")
+
+    def router_logits(self, x: torch.Tensor, router_weight: torch.Tensor, *, out=None, stream=None) -> torch.Tensor:
+        """bf16(x . router_weight^T) with fp32 accumulation: the reference's
+        `self.gate(hidden_states)` (nano_ktrans/models/mixtral.py:127, :212)."""
+        t = self._check_tokens(x)
+        self._check_router(router_weight)
+        xc = x.contiguous()
+        if out is None:
+            out = torch.empty(t, self.num_experts, dtype=torch.bfloat16, device=self.device)
+        elif (not self._on_device(out) or out.dtype != torch.bfloat16 or tuple(out.shape) != (t, self.num_experts)
+              or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous bf16 [{t}, {self.num_experts}] tensor on {self.device}")
+        _lib.check(_lib.lib().moe_router_logits(self._h, xc.data_ptr(), router_weight.data_ptr(), t, out.data_ptr(),
+                                                _stream_handle(stream)), self._h, "moe_router_logits")
+        return out
+
+    def forward_x(self, x: torch.Tensor, router_weight: torch.Tensor, *, out=None, out_ids=None, out_weights=None,
+                  out_logits=None, stream=None) -> torch.Tensor:
+        """The MoE block from hidden states: router projection, routing, routed
+        experts and combine (models/mixtral.py:212-218 with every expert on
+        this backend).  out_logits, when given, receives the router logits."""
+        t = self._check_tokens(x)
+        self._check_router(router_weight)
+        self._check_routing_out(t, out_ids, out_weights)
+        if out_logits is not None:
+            self._check_logits(out_logits, t)
+            if not out_logits.is_contiguous():
+                raise ValueError("out_logits must be contiguous")
+        xc = x.contiguous()
+        out = self._out_for(xc, out)
+        _lib.check(_lib.lib().moe_forward_x(self._h, xc.data_ptr(), router_weight.data_ptr(), t, out.data_ptr(),
+                                            _ptr(out_ids), _ptr(out_weights), _ptr(out_logits),
+                                            _stream_handle(stream)), self._h, "moe_forward_x")
+        return out
+
     def dequant_rows(self, proj: int, expert: int, row0: int, nrows: int, stream=None) -> torch.Tensor:
         k = self.hidden_size if proj in (0, 1, 3, 4) else (self.inter_size if proj == 2 else
                                                             self.weights.shared_inter)
@@ -193,6 +234,13 @@ class MoeLayer:
         """Expert projections of the multi-kernel path: 0 matvec only, 1 tensor-core
         grouped GEMM for large batches (default), 2 grouped GEMM for every batch."""
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_GEMM, int(mode)), self._h, "moe_set_option")
+
+    def set_stream(self, enabled: bool) -> None:
+        """Expert projections of the multi-kernel path below the GEMM threshold:
+        True (default) the weight-streaming tensor-core kernels where the layer's
+        shapes allow, False the CUDA-core matvec kernels."""
+        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_STREAM, int(bool(enabled))), self._h,
+                   "moe_set_option")
 
     def set_gemm_tile(self, width: int) -> None:
         """Token-tile width of the grouped GEMM: 0 chooses by batch, else 16, 32, 64 or 128."""

@@ -215,3 +215,16 @@ def test_moe_layer_rejects_bad_routing_buffers(which, monkeypatch):
     if "logits" not in which:
         with pytest.raises(ValueError):
             lay.route(lg, **kw)
+
+
+def test_is_moe_layer_follows_reference_config_rule():
+    """models/config.py:184-197: dense below first_k_dense_replace, in
+    mlp_only_layers, off the decoder_sparse_step grid, or without experts."""
+    from nano_ktrans_b200.dense_mlp import is_moe_layer
+
+    assert is_moe_layer(0) and is_moe_layer(5)
+    assert not is_moe_layer(0, first_k_dense_replace=1) and is_moe_layer(1, first_k_dense_replace=1)
+    assert not is_moe_layer(3, mlp_only_layers=[3])
+    assert [is_moe_layer(i, decoder_sparse_step=2) for i in range(4)] == [False, True, False, True]
+    assert not is_moe_layer(2, num_local_experts=0) and not is_moe_layer(2, num_experts_per_tok=0)
+    assert not is_moe_layer(2, attention_backend="mla")
