@@ -71,6 +71,9 @@ def parse_args():
     ap.add_argument("--trace", action="store_true",
                     help="after the timed region, record the single-token kernel's per-CTA phase stamps "
                          "and add their median / slowest-CTA times to the JSON line")
+    ap.add_argument("--ncu-case", type=int, default=0,
+                    help="small profiling workload: this many tokens per step through MoeLayer.forward over 4 "
+                         "distinct Qwen3-shaped layers (1.2 GB of weights), 2 passes, then exit")
     ap.add_argument("--skip-decode", action="store_true",
                     help="report only the prefill workloads (profiling runs of the grouped GEMM)")
     return ap.parse_args()
@@ -350,6 +353,31 @@ def run_e2e(layers, x, logits, steps, call=None):
 # ---------------------------------------------------------------------------
 
 
+def run_e2e_host(layers, x, logits, steps):
+    """The C-ABI host-buffer call: moe_forward_host per step (H2D of x and the
+    logits, the step, D2H of the output, all on the stream) from pinned
+    buffers."""
+    import torch
+
+    L = len(layers)
+    xh = x.cpu().pin_memory()
+    lh = logits.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for i in range(2 * L):
+        layers[i % L].forward_host(xh[i % L], lh[i % L], oh[i % L])
+    torch.cuda.synchronize()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        layers[i % L].forward_host(xh[i % L], lh[i % L], oh[i % L])
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1), xh[0].numel() * 2 + lh[0].numel() * 2, oh[0].numel() * 2
+
+
 def hybrid_layers(lws, device):
     """HybridMoE layers (the reference's layer class and forward contract) over
     the same weights, every expert offloaded to the cuda backend."""
@@ -551,6 +579,8 @@ def main():
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=dev).manual_seed(args.seed + 1000 * rank)
+    if args.ncu_case:
+        return ncu_case(gen, dev, args.ncu_case)
     if args.skip_decode:
         pre = prefill_block(args, dev, rank)
         if rank == 0:
@@ -626,11 +656,17 @@ def main():
         line["phase_timeline_us"] = trace_phases(layers, x, logits, outs, clk.summary().get("sm_mhz") or 1965.0)
 
     if not args.no_e2e:
-        e_ms, h2d, d2h = run_e2e(layers, x, logits, args.e2e_steps)
+        e_ms, h2d, d2h = run_e2e_host(layers, x, logits, args.e2e_steps)
         e_ms = max_over_ranks(e_ms)
         line["e2e"] = {"value": args.e2e_steps * args.batch * world / (e_ms / 1e3), "unit": "tokens/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
-                       "api": "MoeLayer.forward per step, eager (pinned host buffers)"}
+                       "api": "moe_forward_host per step (C ABI via MoeLayer.forward_host): pinned host x and "
+                              "logits in, bf16 output back to pinned host memory"}
+        t_ms, _, _ = run_e2e(layers, x, logits, args.e2e_steps)
+        t_ms = max_over_ranks(t_ms)
+        line["e2e"]["moe_layer_forward"] = {
+            "value": args.e2e_steps * args.batch * world / (t_ms / 1e3), "unit": "tokens/s",
+            "api": "torch copies of pinned host tensors + MoeLayer.forward on device tensors, per step"}
         if args.batch == 1:
             hyb = hybrid_layers(lws, dev)
 
@@ -947,6 +983,31 @@ def run_prefill(name: str, gen, device, steps: int, warmup: int, cpu_seconds: fl
     return res
 
 
+def ncu_case(gen, dev, batch: int, n_layers: int = 4, passes: int = 2):
+    """A small, bounded workload for kernel captures: `passes` eager passes of
+    MoeLayer.forward over n_layers distinct Qwen3-shaped W4 layers at `batch`
+    tokens (launch i of a kernel class belongs to layer i % n_layers)."""
+    import torch
+
+    from nano_ktrans_b200.moe_layer import MoeLayer
+
+    lws = [make_unique_layer(gen, dev) for _ in range(n_layers)]
+    layers = [MoeLayer(lw, top_k=CFG["top_k"], router_use_softmax=True, normalize_topk_prob=True, max_tokens=batch)
+              for lw in lws]
+    x, logits = make_inputs(gen, n_layers, batch, dev)
+    out = torch.empty_like(x)
+    for _ in range(passes):
+        for i, lay in enumerate(layers):
+            lay.forward(x[i], logits[i], out=out[i])
+    torch.cuda.synchronize()
+    bad = sum(lay.read_status() for lay in layers)
+    print(json.dumps({"ncu_case": batch, "layers": n_layers, "passes": passes,
+                      "launches_per_step": layers[0].last_launch_count(), "status": bad}), flush=True)
+    for lay in layers:
+        lay.close()
+    return 0 if bad == 0 else 1
+
+
 def run_m32_bmm(gen, device, steps: int, warmup: int, n_layers: int = 4):
     """The reference's GPU-resident batch-1 comparator (the fused stacked-bmm
     decode of hybrid_moe.py:3442-3500) restated in PyTorch on dense bf16
@@ -1261,4 +1322,4 @@ def read_traffic(kernel: str, batch: int):
 
 
 if __name__ == "__main__":
-    main()
+    sys.exit(main() or 0)

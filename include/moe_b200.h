@@ -17,6 +17,10 @@
  *                        index_add_ combine cpu_moe.py:528-538)
  *   moe_forward          HybridMoE.forward with every expert offloaded
  *                        (hybrid_moe.py:3310-3570): route + experts
+ *   moe_forward_host     moe_forward on host buffers: the step the reference's
+ *                        CPU backend serves from host copies of the hidden
+ *                        states (hybrid_moe.py:3373-3378, cpu_moe.py:491-539),
+ *                        here copied to the device and back on the stream
  *   moe_router_logits    the router projection `self.gate(hidden_states)`
  *                        nano_ktrans/models/mixtral.py:127, :212 (bf16
  *                        nn.Linear, no bias)
@@ -139,6 +143,14 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
                 int32_t num_tokens, uint16_t* out_dev, int64_t* topk_ids_dev,
                 uint16_t* topk_weights_dev, void* stream);
 
+/* moe_forward with HOST buffers: x_host [T, H] and logits_host [T, E] bf16
+ * are copied into the handle's workspace, the step runs, and the bf16 output
+ * is copied back into out_host [T, H] — all enqueued on `stream`; the output
+ * is valid once the stream reaches that point.  The host buffers should be
+ * page-locked (pageable memory makes the copies synchronous). */
+int moe_forward_host(void* handle, const uint16_t* x_host, const uint16_t* logits_host,
+                     int32_t num_tokens, uint16_t* out_host, void* stream);
+
 /* Router logits [T, E] bf16 = bf16(x [T, H] . router_w [E, H]^T), fp32
  * accumulation (the reference's bf16 nn.Linear gate).  x_dev and
  * router_w_dev 16-byte aligned; hidden_size a multiple of 32. */
@@ -221,8 +233,10 @@ enum moe_option {
   /* 1: the single-launch decode kernels record per-CTA phase stamps
    * (allocates num_SMs * 16 * 8 bytes); read them with moe_read_trace. */
   MOE_OPT_TRACE = 2,
-  /* Expert projections of the multi-kernel path: 0 = matvec kernels only;
-   * 1 (default) = tensor-core grouped GEMM once T * top_k >= 4 * num_experts;
+  /* Expert projections of the multi-kernel path: 0 = no GEMM (streaming or
+   * matvec kernels, see MOE_OPT_STREAM); 1 (default) = tensor-core grouped
+   * GEMM once T * top_k >= 16 * num_experts where the streaming kernels apply
+   * (>= 4 * num_experts elsewhere);
    * 2 = grouped GEMM for every batch the single-launch kernel does not take.
    * The GEMM path needs inter and hidden multiples of 128 and, for W4,
    * group_size a multiple of 64 (W8: per-channel); value 2 on another shape

@@ -50,6 +50,7 @@ SIGNATURES = {
     "moe_route": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "moe_experts_forward": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp]),
     "moe_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "moe_forward_host": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
     "moe_router_logits": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
     "moe_forward_x": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
     "moe_dequant_rows": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp]),

@@ -37,7 +37,9 @@ struct Handle {
   float* sh_h = nullptr;   // [max_tokens][I_s]
   float* sh_y = nullptr;   // [max_tokens][H]
   float* sh_g = nullptr;   // [max_tokens]
-  uint16_t* logits_tmp = nullptr;  // [max_tokens][E] router logits of moe_forward_x
+  uint16_t* logits_tmp = nullptr;  // [max_tokens][E] router logits of moe_forward_x / moe_forward_host
+  uint16_t* x_stage = nullptr;     // [max_tokens][H] moe_forward_host input
+  uint16_t* out_stage = nullptr;   // [max_tokens][H] moe_forward_host output
   int64_t* ids_tmp = nullptr;
   uint16_t* w_tmp = nullptr;
   unsigned long long* grid_bar = nullptr;  // grid-barrier arrival counter of the fused decode kernel
@@ -201,10 +203,12 @@ int pick_bn(int pairs, int experts) {
   return mean <= 16 ? 16 : mean <= 32 ? 32 : mean <= 64 ? 64 : 128;
 }
 
-bool use_gemm(const Handle* h, int pairs) {
+// With the weight-streaming kernels available the GEMM takes over once the
+// mean expert sees two full 8-token chunks; without them, at half that.
+bool use_gemm(const Handle* h, int pairs, bool stream_ok) {
   if (!h->gemm_maps || h->gemm_mode == 0) return false;
   if (h->gemm_mode == 2) return true;
-  return pairs >= 4 * h->d.num_experts;
+  return pairs >= (stream_ok ? 16 : 4) * h->d.num_experts;
 }
 
 }  // namespace
@@ -239,7 +243,8 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
                o_nact = take(4), o_sorted = take(4 * P), o_pos = take(4 * P), o_h = take(4 * P * I),
                o_y = take(4 * P * H), o_shh = take(S ? 4 * T * S : 0), o_shy = take(S ? 4 * T * H : 0),
                o_shg = take(S ? 4 * T : 0), o_ids = take(8 * P), o_w = take(2 * P), o_bar = take(8),
-               o_tiles = take(4 * (E + 1)), o_shtab = take(4 * 8), o_gids = take(8 * P), o_lg = take(2 * T * E);
+               o_tiles = take(4 * (E + 1)), o_shtab = take(4 * 8), o_gids = take(8 * P), o_lg = take(2 * T * E),
+               o_xs = take(2 * T * H), o_os = take(2 * T * H);
   h->ws_bytes = off;
   cudaError_t e = cudaMalloc(&h->ws, h->ws_bytes);
   if (e != cudaSuccess) {
@@ -269,6 +274,8 @@ int moe_create(const moe_layer_desc* desc, void** handle, char* err, size_t err_
   h->sh_tables = reinterpret_cast<int32_t*>(b + o_shtab);
   h->slot_ids = reinterpret_cast<int64_t*>(b + o_gids);
   h->logits_tmp = reinterpret_cast<uint16_t*>(b + o_lg);
+  h->x_stage = reinterpret_cast<uint16_t*>(b + o_xs);
+  h->out_stage = reinterpret_cast<uint16_t*>(b + o_os);
   e = cudaMemset(h->ws, 0, h->ws_bytes);
   if (e != cudaSuccess) {
     fmt_err(err, err_len, "moe_create: cudaMemset failed: %s", cudaGetErrorString(e));
@@ -428,7 +435,8 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     return fail(h, MOE_EINVAL, "GEMM path forced but this layer's shape is outside its rules");
   const bool shared_gemm = add_shared && d.shared_inter > 0 && h->shared_gemm_maps && h->gemm_mode != 0 &&
                            (h->gemm_mode == 2 || T >= 16);
-  const bool routed_gemm = use_gemm(h, T * k);
+  const bool stream_ok = h->stream_mode && moe::stream_eligible(d.bits, gate, up, down, max_active);
+  const bool routed_gemm = use_gemm(h, T * k, stream_ok);
   const int bn = h->gemm_tile ? h->gemm_tile : pick_bn(T * k, E);
   const int sbn = h->gemm_tile ? h->gemm_tile : pick_bn(T, 1);
   if (routed_gemm || shared_gemm) {
@@ -467,9 +475,10 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     prof_mark(h, MOE_K_DOWN, true, st);
     if (rc < 0) return fail(h, MOE_ECUDA, "grouped GEMM (down): shared-memory opt-in refused");
     launches += 2;
-  } else if (h->stream_mode && moe::stream_eligible(d.bits, gate, up, down, max_active)) {
+  } else if (stream_ok) {
     prof_mark(h, MOE_K_GATEUP, false, st);
-    int rc = moe::launch_stream_gateup(x, h->rt, k, max_active, gate, up, h->hbuf, h->rt.status, h->num_sms, st);
+    int rc = moe::launch_stream_gateup(x, h->rt, k, max_active, gate, up, h->hbuf, h->rt.status, h->trace,
+                                       h->num_sms, st);
     prof_mark(h, MOE_K_GATEUP, true, st);
     if (rc < 0) return fail(h, MOE_ECUDA, "streaming gate/up: launch refused");
     prof_mark(h, MOE_K_DOWN, false, st);
@@ -580,6 +589,26 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
                     h->d.normalize_topk_prob != 0, ids, wts, st);
   prof_mark(h, MOE_K_ROUTE, true, st);
   return experts_forward(h, x_dev, ids, wts, T, nullptr, true, out_dev, st, 1);
+}
+
+int moe_forward_host(void* handle, const uint16_t* x_host, const uint16_t* logits_host, int32_t T,
+                     uint16_t* out_host, void* stream) {
+  Handle* h = static_cast<Handle*>(handle);
+  if (h == nullptr) return MOE_EINVAL;
+  if (int rc = check_forward_args(h, x_host, out_host, T)) return rc;
+  if (T > 0 && logits_host == nullptr) return fail(h, MOE_EINVAL, "null logits pointer");
+  h->last_launches = 0;
+  if (T == 0) return MOE_OK;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t xb = sizeof(uint16_t) * static_cast<size_t>(T) * h->d.hidden_size;
+  const size_t lb = sizeof(uint16_t) * static_cast<size_t>(T) * h->d.num_experts;
+  if (cudaMemcpyAsync(h->x_stage, x_host, xb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(h->logits_tmp, logits_host, lb, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return fail(h, MOE_ECUDA, "moe_forward_host: input copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if (int rc = moe_forward(handle, h->x_stage, h->logits_tmp, T, h->out_stage, nullptr, nullptr, stream)) return rc;
+  if (cudaMemcpyAsync(out_host, h->out_stage, xb, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return fail(h, MOE_ECUDA, "moe_forward_host: output copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return MOE_OK;
 }
 
 int moe_router_logits(void* handle, const uint16_t* x_dev, const uint16_t* router_w_dev, int32_t T,

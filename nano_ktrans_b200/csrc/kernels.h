@@ -58,7 +58,8 @@ int launch_down(int bits, const float* h, const RouteTables& rt, int max_active,
 // return 1 when launched, negative when not.
 bool stream_eligible(int bits, const QuantProj& gate, const QuantProj& up, const QuantProj& down, int max_active);
 int launch_stream_gateup(const uint16_t* x, const RouteTables& rt, int top_k, int max_active, const QuantProj& gate,
-                         const QuantProj& up, float* h, int* status, int num_sms, cudaStream_t st);
+                         const QuantProj& up, float* h, int* status, unsigned long long* trace, int num_sms,
+                         cudaStream_t st);
 int launch_stream_down(const float* h, const RouteTables& rt, int max_active, const QuantProj& down, float* y,
                        int* status, int num_sms, cudaStream_t st);
 

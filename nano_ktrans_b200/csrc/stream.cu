@@ -25,24 +25,31 @@
 // of items, so a CTA sees one or two chunks and streams their rows in order.
 //
 // Warp roles, one CTA per SM:
-//   warps 0-7  consumers.  The 8 warps are P K-parts x (8 / P) row sets; warp
-//              w takes K-part w % P (the 128-code groups p, p + P, ...) of two
-//              16-row tiles of set w / P.  Gate/up: a set is 16 gate rows and
-//              the same 16 up rows (R = 16 * sets).  Down: a set is 32 rows
-//              (R = 32 * sets).  A warp keeps its K-part's B fragments in
-//              registers for the whole chunk; the P partial sums of an output
-//              meet in shared memory and are added in part order, so results
-//              do not depend on timing.
-//   warp 8     producer.  One lane issues, per item, the bulk copies of its
-//              code rows and scale rows into the next ring stage.
-//   warp 9     operand stager.  Converts each chunk's activations (gate/up:
-//              bf16 x rows of its tokens; down: fp32 h rows) into B-fragment
-//              order with the per-group corrections, while the consumers work
-//              on the previous chunk.
+//   warps 0-15  consumers.  The 16 warps are P K-parts x (16 / P) 16-row
+//               tiles: warp w computes tile w / P of the item over the
+//               128-code groups p, p + P, ... of K-part p = w % P.  Gate/up
+//               tiles alternate gate and up rows (R = 8 * 16 / P); down tiles
+//               are consecutive rows (R = 16 * 16 / P).  A warp keeps its
+//               K-part's B fragments in registers for the whole chunk.
+//   warp 16     producer: one lane issues, per item, the bulk copies of its
+//               code rows and scale rows into the next ring stage.
+//   warp 17     rows + epilogue.  Bulk-copies each chunk's activation rows
+//               (gate/up: the bf16 x rows of its tokens; down: the fp32 h
+//               rows) into a shared-memory area once the consumers have taken
+//               the previous chunk's (each consumer warp builds its B fragments
+//               and per-group corrections from those rows once per chunk;
+//               down splits h into its bf16 hi + lo terms).  Per item, adds
+//               the P partial sums of each output in part order (results do
+//               not depend on timing), applies SiLU(g) * u for gate/up, and
+//               stores the outputs.
+// The consumers pass partial sums to the epilogue through a ring of
+// shared-memory buffers, so no consumer waits for another.
 //
-// Every wait is bounded.  A wait that runs out sets the CTA's abort flag and
-// the status word (kStatusTimeout); consumers leave together through a
-// reducing barrier, the producer waits (bounded) for its copies in flight.
+// Every wait is bounded (2 s of %globaltimer; while waiting, a warp is
+// suspended on the mbarrier rather than spinning).  A wait that runs out sets
+// the CTA's abort flag and the status word (kStatusTimeout); every role then
+// leaves, the producer and the stager after their copies in flight have landed
+// (bounded as well).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -55,15 +62,23 @@
 namespace moe {
 namespace sm {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 64;  // + producer warp + operand warp
-constexpr int kTok = 8;                    // tokens per chunk: the mma's N
+constexpr int kConsumerWarps = 16;
+constexpr int kProducerWarp = 16, kEpilogueWarp = 17, kEpilogueWarps = 2;
+constexpr int kThreads = (kEpilogueWarp + kEpilogueWarps) * 32;
+constexpr int kTok = 8;  // tokens per chunk: the mma's N
 constexpr int kMaxStages = 8;
-constexpr int kRedPitch = 17;                      // floats per (tile, token) row of the partial-sum buffer
-constexpr int kRedTile = kTok * kRedPitch;         // floats per tile
-constexpr int kRedFloats = 16 * kRedTile;          // P * tiles == 16 in every configuration
+constexpr int kRedBufs = 3;
+// A partial-sum buffer holds red[token][item row][K-part]: the P partials of
+// one output are adjacent (vector loads in the epilogue).  Item rows x P is
+// 256 in every configuration (gate/up: 2R rows, R = 128 / P; down: R = 256 / P).
+constexpr int kRedRowParts = 256;
+constexpr int kRedFloats = kTok * kRedRowParts;
 constexpr int kSmemLimit = 227 * 1024;
+// mbarriers: full[kMaxStages], empty[kMaxStages], red_full[kRedBufs], red_empty[kRedBufs], xfull, xempty, raw
+constexpr int kBarFull = 0, kBarEmpty = kMaxStages, kBarRedFull = 2 * kMaxStages,
+              kBarRedEmpty = 2 * kMaxStages + kRedBufs, kBarXEmpty = 2 * kMaxStages + 2 * kRedBufs,
+              kBarRaw = kBarXEmpty + 1, kNumBars = kBarXEmpty + 2;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 struct Args {
   const uint16_t* x;  // gate/up: bf16 [T][K]
@@ -76,6 +91,7 @@ struct Args {
   QuantProj p0, p1;  // gate, up | down
   float* out;        // gate/up: SiLU(g)*u [pairs][N]; down: y [pairs][N]
   int* status;
+  unsigned long long* trace;  // optional [G][16] %globaltimer stamps (gate/up launch), see kTrace*
   int parts;         // P
   int rows;          // R: output rows per item
   int stages;
@@ -85,27 +101,35 @@ struct Args {
   uint32_t scale_bytes;  // scale bytes of one item
 };
 
+// Trace slots per CTA (ns): 0 entry (absolute), then offsets from entry:
+// 1 chunk table built, 2 first operands ready (consumer warp 0), 3 consumer
+// warp 0 done, 4 producer done, 5 epilogue done; 6 the CTA's item count.
+#define STREAM_TRACE(slot, t0)                                                      \
+  do {                                                                            \
+    if (a.trace != nullptr)                                                       \
+      a.trace[blockIdx.x * 16 + (slot)] = (slot) == 0 ? (t0) : ac::global_ns() - (t0); \
+  } while (0)
+
 struct Smem {
   // byte offsets into dynamic shared memory
-  uint32_t tab, corr, xbuf, red, stage;
+  uint32_t tab, raw, red, stage;
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
+// Bytes of one activation row as stored in global memory (bf16 x | fp32 h).
 template <bool GATEUP>
-__host__ __device__ inline uint32_t xbuf_bytes(int K) {
-  return static_cast<uint32_t>(kTok) * K * (GATEUP ? 2 : 4);  // bf16 x | bf16 hi + lo
+__host__ __device__ inline uint32_t row_bytes(int K) {
+  return static_cast<uint32_t>(K) * (GATEUP ? 2 : 4);
 }
 
 template <bool GATEUP>
 __host__ __device__ inline Smem smem_layout(int K, int max_active) {
   Smem s;
-  const uint32_t bars = 160;  // (2 * kMaxStages + 2) mbarriers, then the abort flag
-  s.tab = bars;
-  s.corr = align_up(s.tab + 4u * 4u * (max_active + 1), 16);
-  s.xbuf = align_up(s.corr + 4u * kTok * (K / 128), 128);
-  s.red = align_up(s.xbuf + xbuf_bytes<GATEUP>(K), 128);
-  s.stage = align_up(s.red + 2u * 4u * kRedFloats, 128);
+  s.tab = align_up(8u * kNumBars + 4u, 16);  // mbarriers, then the abort flag
+  s.raw = align_up(s.tab + 4u * 4u * (max_active + 1), 128);
+  s.red = align_up(s.raw + kTok * row_bytes<GATEUP>(K), 128);
+  s.stage = align_up(s.red + 4u * kRedBufs * kRedFloats, 128);
   return s;
 }
 
@@ -115,79 +139,82 @@ MOE_DEV void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Wait for phase `parity` of `bar`; false if the CTA aborted or the wait ran out
-// (which aborts it).
-MOE_DEV bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  for (uint32_t i = 0;; ++i) {
-    if (ac::mbar_try_wait(bar, parity)) return true;
-    if ((i & 31u) == 31u && *abort_flag) return false;
-    if (i > ac::kSpinLimit) {
-      *abort_flag = 1;
-      return false;
+// try_wait with a suspend-time hint: the warp sleeps on the barrier (up to
+// `ns`) instead of re-polling.
+MOE_DEV bool try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar`; false if the CTA aborted or the wait ran
+// out of its time limit (which aborts it).
+MOE_DEV bool wait_phase_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  const unsigned long long t0 = ac::global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (try_wait_sleep(bar, parity, 20000u)) return true;
+    if ((i & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (ac::global_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
 }
 
-// Barrier over the consumer warps that also ORs a flag across them.
-MOE_DEV bool consumers_sync_or(bool flag) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n}"
-      : "=r"(out)
-      : "r"(static_cast<uint32_t>(flag)), "n"(kConsumers)
-      : "memory");
-  return out != 0;
+MOE_DEV bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  return ac::mbar_try_wait(bar, parity) || wait_phase_slow(bar, parity, abort_flag);
 }
 
-// One 128-code group of a 16-row tile against 8 token columns: wlo / whi are
-// the lane's 16 code bytes of tile rows g and g + 8, b[q] the operand words of
-// step pair q (mma_gemv.cuh order).  d[0..1]: row g, tokens 2t, 2t+1; d[2..3]:
-// row g + 8.
-MOE_DEV void group_x(uint4 wlo, uint4 whi, uint4 b0, uint4 b1, uint4 b2, uint4 b3, float (&d)[4]) {
-  constexpr uint32_t M = 0x43004300u, N = 0x000F000Fu;
-  const uint4 b[4] = {b0, b1, b2, b3};
-  const uint32_t u[4] = {wlo.x, wlo.y, wlo.z, wlo.w};
-  const uint32_t v[4] = {whi.x, whi.y, whi.z, whi.w};
-  float e[4][4];
-#pragma unroll
-  for (int s = 0; s < 4; ++s) e[s][0] = e[s][1] = e[s][2] = e[s][3] = 0.0f;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    mma16816_bf16(e[(2 * q) & 3], (u[q] & N) | M, (v[q] & N) | M, ((u[q] >> 4) & N) | M, ((v[q] >> 4) & N) | M,
-                  b[q].x, b[q].y);
-    mma16816_bf16(e[(2 * q + 1) & 3], ((u[q] >> 8) & N) | M, ((v[q] >> 8) & N) | M, ((u[q] >> 12) & N) | M,
-                  ((v[q] >> 12) & N) | M, b[q].z, b[q].w);
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r) d[r] = (e[0][r] + e[1][r]) + (e[2][r] + e[3][r]);
+// Bounded wait that ignores the abort flag: for copies in flight that must land
+// before the CTA exits.
+MOE_DEV void wait_landed(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = ac::global_ns();
+  while (!try_wait_sleep(bar, parity, 20000u))
+    if (ac::global_ns() - t0 > kWaitLimitNs) return;
 }
 
-// The same with a two-term operand: bh = bf16 hi words, bl = lo words.
-MOE_DEV void group_hl(uint4 wlo, uint4 whi, const uint4* bh, const uint4* bl, float (&d)[4]) {
-  constexpr uint32_t M = 0x43004300u, N = 0x000F000Fu;
-  const uint32_t u[4] = {wlo.x, wlo.y, wlo.z, wlo.w};
-  const uint32_t v[4] = {whi.x, whi.y, whi.z, whi.w};
-  float e[4][4];
-#pragma unroll
-  for (int s = 0; s < 4; ++s) e[s][0] = e[s][1] = e[s][2] = e[s][3] = 0.0f;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t a0 = (u[q] & N) | M, a1 = (v[q] & N) | M, a2 = ((u[q] >> 4) & N) | M, a3 = ((v[q] >> 4) & N) | M;
-    const uint32_t c0 = ((u[q] >> 8) & N) | M, c1 = ((v[q] >> 8) & N) | M, c2 = ((u[q] >> 12) & N) | M,
-                   c3 = ((v[q] >> 12) & N) | M;
-    mma16816_bf16(e[0], a0, a1, a2, a3, bh[q].x, bh[q].y);
-    mma16816_bf16(e[1], a0, a1, a2, a3, bl[q].x, bl[q].y);
-    mma16816_bf16(e[2], c0, c1, c2, c3, bh[q].z, bh[q].w);
-    mma16816_bf16(e[3], c0, c1, c2, c3, bl[q].z, bl[q].w);
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r) d[r] = (e[0][r] + e[1][r]) + (e[2][r] + e[3][r]);
+// The lanes' earlier shared-memory stores, then one arrival for the warp.
+MOE_DEV void warp_arrive(uint32_t bar) {
+  __threadfence_block();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
 // (x0, x4) (x1, x5) (x2, x6) (x3, x7) operand words of 8 values given as bf16 bits.
 MOE_DEV uint4 pack_pairs(uint32_t p01, uint32_t p23, uint32_t p45, uint32_t p67) {
   return make_uint4(__byte_perm(p01, p45, 0x5410), __byte_perm(p01, p45, 0x7632), __byte_perm(p23, p67, 0x5410),
                     __byte_perm(p23, p67, 0x7632));
+}
+
+// A-operand registers of code word pair (u: tile row g, v: row g + 8): steps
+// 2q (nibbles 0,4 / 1,5) and 2q + 1 (nibbles 2,6 / 3,7), as 128 + q bf16.
+struct AWords {
+  uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
+};
+// (x & 0x000F000F) | 0x43004300 as one LOP3 (LUT 0xEA = (a & b) | c).
+MOE_DEV uint32_t nib_bf16(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "n"(0x000F000F), "r"(0x43004300u));
+  return r;
+}
+MOE_DEV AWords unpack_a(uint32_t u, uint32_t v) {
+  AWords w;
+  w.a0 = nib_bf16(u);
+  w.a1 = nib_bf16(v);
+  w.a2 = nib_bf16(u >> 4);
+  w.a3 = nib_bf16(v >> 4);
+  w.c0 = nib_bf16(u >> 8);
+  w.c1 = nib_bf16(v >> 8);
+  w.c2 = nib_bf16(u >> 12);
+  w.c3 = nib_bf16(v >> 12);
+  return w;
 }
 
 struct ChunkRef {
@@ -212,6 +239,55 @@ struct Cursor {
   }
 };
 
+// One consumer warp's share of an item: its NV groups (all valid: no per-group
+// guards in the unrolled body) of one 16-row tile against the chunk's tokens.
+// Reads the stage (codes + scales), then releases it (`release` runs once the
+// stage's words are in registers); returns the tile's partial sums in acc.
+template <bool GATEUP, int NV, int GPW, typename Release>
+MOE_DEV void item_compute(const unsigned char* st, const uint16_t* sc, const uint32_t (&woff)[GPW],
+                          const uint32_t (&soff)[GPW], uint32_t w8, uint32_t s8,
+                          const uint4 (&bx)[GPW][GATEUP ? 4 : 8], const float (&cx)[GPW][2], Release release,
+                          float (&acc)[4]) {
+  uint4 wlo[NV], whi[NV];
+  float slo[NV], shi[NV];
+#pragma unroll
+  for (int gi = 0; gi < NV; ++gi) {
+    wlo[gi] = lds128(st + woff[gi]);
+    whi[gi] = lds128(st + woff[gi] + w8);
+    slo[gi] = bf16_to_f32(sc[soff[gi]]);
+    shi[gi] = bf16_to_f32(sc[soff[gi] + s8]);
+  }
+  release();
+  // NV independent accumulator pairs (even / odd steps), interleaved per word
+  float e[NV][2][4];
+#pragma unroll
+  for (int gi = 0; gi < NV; ++gi)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) e[gi][h][0] = e[gi][h][1] = e[gi][h][2] = e[gi][h][3] = 0.0f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int gi = 0; gi < NV; ++gi) {
+      const uint32_t u = q == 0 ? wlo[gi].x : q == 1 ? wlo[gi].y : q == 2 ? wlo[gi].z : wlo[gi].w;
+      const uint32_t v = q == 0 ? whi[gi].x : q == 1 ? whi[gi].y : q == 2 ? whi[gi].z : whi[gi].w;
+      const AWords A = unpack_a(u, v);
+      mma16816_bf16(e[gi][0], A.a0, A.a1, A.a2, A.a3, bx[gi][q].x, bx[gi][q].y);
+      mma16816_bf16(e[gi][1], A.c0, A.c1, A.c2, A.c3, bx[gi][q].z, bx[gi][q].w);
+      if constexpr (!GATEUP) {
+        mma16816_bf16(e[gi][0], A.a0, A.a1, A.a2, A.a3, bx[gi][q + 4].x, bx[gi][q + 4].y);
+        mma16816_bf16(e[gi][1], A.c0, A.c1, A.c2, A.c3, bx[gi][q + 4].z, bx[gi][q + 4].w);
+      }
+    }
+  }
+#pragma unroll
+  for (int gi = 0; gi < NV; ++gi) {
+    acc[0] = fmaf(slo[gi], (e[gi][0][0] + e[gi][1][0]) - cx[gi][0], acc[0]);
+    acc[1] = fmaf(slo[gi], (e[gi][0][1] + e[gi][1][1]) - cx[gi][1], acc[1]);
+    acc[2] = fmaf(shi[gi], (e[gi][0][2] + e[gi][1][2]) - cx[gi][0], acc[2]);
+    acc[3] = fmaf(shi[gi], (e[gi][0][3] + e[gi][1][3]) - cx[gi][1], acc[3]);
+  }
+}
+
 template <bool GATEUP, int GPW>
 __global__ void __launch_bounds__(kThreads, 1) stream_kernel(Args a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -220,36 +296,43 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(Args a) {
   const int P = a.parts, S = a.stages, R = a.rows;
   const Smem L = smem_layout<GATEUP>(K, a.max_active);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  const uint32_t full0 = ac::smem_u32(&bars[0]), empty0 = ac::smem_u32(&bars[kMaxStages]);
-  const uint32_t xfull = ac::smem_u32(&bars[2 * kMaxStages]), xempty = ac::smem_u32(&bars[2 * kMaxStages + 1]);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 8 * (2 * kMaxStages + 2));
+  const uint32_t bar0 = ac::smem_u32(&bars[0]);
+  auto bar = [bar0](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 8 * kNumBars);
   int* tab = reinterpret_cast<int*>(smem + L.tab);
-  float* cb = reinterpret_cast<float*>(smem + L.corr);  // [kTok][nG] 136 * sum of the operand per group
-  uint4* xb = reinterpret_cast<uint4*>(smem + L.xbuf);
+  const unsigned char* raw = smem + L.raw;  // [kTok][K] activation rows of the current chunk
   float* red = reinterpret_cast<float*>(smem + L.red);
   unsigned char* stages = smem + L.stage;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const unsigned long long t_entry = ac::global_ns();
+  if (threadIdx.x == 0) STREAM_TRACE(0, t_entry);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      ac::mbar_init(full0 + 8 * s, 1);
-      ac::mbar_init(empty0 + 8 * s, kConsumerWarps);
+      ac::mbar_init(bar(kBarFull + s), 1);
+      ac::mbar_init(bar(kBarEmpty + s), kConsumerWarps);
     }
-    ac::mbar_init(xfull, 32);
-    ac::mbar_init(xempty, kConsumerWarps);
+    for (int b = 0; b < kRedBufs; ++b) {
+      ac::mbar_init(bar(kBarRedFull + b), kConsumerWarps);
+      ac::mbar_init(bar(kBarRedEmpty + b), kEpilogueWarps);
+    }
+    ac::mbar_init(bar(kBarXEmpty), kConsumerWarps);
+    ac::mbar_init(bar(kBarRaw), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // chunk table: prefix of ceil(count / 8) over the active experts (warp 0)
+  // chunk table: exclusive prefix of ceil(count / 8) over the active experts,
+  // every thread loading one entry (warp totals meet in the first red buffer)
   const int n_act = min(*a.n_active, a.max_active);
   const int cap = a.max_active + 1;
-  if (warp == 0) {
+  {
+    int* wtot = reinterpret_cast<int*>(smem + L.red);
     int run = 0;
-    for (int base = 0; base < n_act; base += 32) {
-      const int i = base + lane;
+    for (int base = 0; base < n_act; base += kThreads) {
+      const int i = base + threadIdx.x;
       int c = 0, e = 0, off = 0, cnt = 0;
       if (i < n_act) {
         e = a.active[i];
@@ -263,17 +346,27 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(Args a) {
         const int v = __shfl_up_sync(kFullMask, inc, d);
         if (lane >= d) inc += v;
       }
+      if (lane == 31) wtot[warp] = inc;
+      __syncthreads();
+      int before = run, all = run;
+      for (int w = 0; w < kThreads / 32; ++w) {
+        const int v = wtot[w];
+        if (w < warp) before += v;
+        all += v;
+      }
       if (i < n_act) {
-        tab[i] = run + inc - c;
+        tab[i] = before + inc - c;
         tab[cap + i] = e;
         tab[2 * cap + i] = off;
         tab[3 * cap + i] = cnt;
       }
-      run += __shfl_sync(kFullMask, inc, 31);
+      run = all;
+      __syncthreads();
     }
-    if (lane == 0) tab[n_act] = run;
+    if (threadIdx.x == 0) tab[n_act] = run;
   }
   __syncthreads();
+  if (threadIdx.x == 0) STREAM_TRACE(1, t_entry);
 
   const int total_chunks = tab[n_act];
   const int blocks = N / R;
@@ -283,222 +376,286 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(Args a) {
   const size_t rowb = static_cast<size_t>(K) / 2;
   const int sstride = a.p0.sstride;
 
-  if (warp == kConsumerWarps) {
+  if (warp == kProducerWarp) {
     // ---------------- producer ----------------
-    if (lane == 0) {
+    if (lane == 0 && hi > lo) {
       Cursor cur{tab, cap};
-      int issued = lo;
+      int gc = lo / blocks, rbk = lo - gc * blocks;
+      ChunkRef c = cur.at(gc);
+      int s = 0, ph = 0, issued = 0;
+      bool failed = false;
+      const uint32_t cpp = static_cast<uint32_t>(R * rowb), spp = static_cast<uint32_t>(R * sstride * 2);
       for (int it = lo; it < hi; ++it) {
-        const int k = it - lo, s = k % S;
-        if (!wait_phase(empty0 + 8 * s, ((k / S) & 1) ^ 1, abort_flag)) break;
-        const ChunkRef c = cur.at(it / blocks);
-        const size_t row0 = static_cast<size_t>(c.e) * N + static_cast<size_t>(it % blocks) * R;
-        const uint32_t dst = ac::smem_u32(stages + static_cast<size_t>(s) * a.stage_bytes);
-        ac::mbar_arrive_expect_tx(full0 + 8 * s, a.code_bytes + a.scale_bytes);
-        const uint32_t cpp = static_cast<uint32_t>(R * rowb), spp = static_cast<uint32_t>(R * sstride * 2);
-        ac::bulk_g2s(dst, a.p0.q + row0 * rowb, cpp, full0 + 8 * s);
-        if constexpr (GATEUP) {
-          ac::bulk_g2s(dst + cpp, a.p1.q + row0 * rowb, cpp, full0 + 8 * s);
-          ac::bulk_g2s(dst + 2 * cpp, a.p0.s + row0 * sstride, spp, full0 + 8 * s);
-          ac::bulk_g2s(dst + 2 * cpp + spp, a.p1.s + row0 * sstride, spp, full0 + 8 * s);
-        } else {
-          ac::bulk_g2s(dst + cpp, a.p0.s + row0 * sstride, spp, full0 + 8 * s);
+        if (!wait_phase(bar(kBarEmpty + s), ph ^ 1, abort_flag)) {
+          failed = true;
+          break;
         }
-        issued = it + 1;
+        const size_t row0 = static_cast<size_t>(c.e) * N + static_cast<size_t>(rbk) * R;
+        const uint32_t dst = ac::smem_u32(stages + static_cast<size_t>(s) * a.stage_bytes);
+        const uint32_t fb = bar(kBarFull + s);
+        ac::mbar_arrive_expect_tx(fb, a.code_bytes + a.scale_bytes);
+        ac::bulk_g2s(dst, a.p0.q + row0 * rowb, cpp, fb);
+        if constexpr (GATEUP) {
+          ac::bulk_g2s(dst + cpp, a.p1.q + row0 * rowb, cpp, fb);
+          ac::bulk_g2s(dst + 2 * cpp, a.p0.s + row0 * sstride, spp, fb);
+          ac::bulk_g2s(dst + 2 * cpp + spp, a.p1.s + row0 * sstride, spp, fb);
+        } else {
+          ac::bulk_g2s(dst + cpp, a.p0.s + row0 * sstride, spp, fb);
+        }
+        ++issued;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+        if (++rbk == blocks && it + 1 < hi) {
+          rbk = 0;
+          c = cur.at(++gc);
+        }
       }
-      // the copies still in flight land before the CTA may exit
-      for (int it = max(lo, issued - S); it < issued; ++it) {
-        const int k = it - lo;
-        ac::mbar_wait_bounded(full0 + 8 * (k % S), (k / S) & 1);
+      // the copies still in flight land before the CTA may exit: the last
+      // min(S, issued) stages, walking back from the next slot
+      for (int j = 0; j < min(S, issued); ++j) {
+        if (--s < 0) {
+          s = S - 1;
+          ph ^= 1;
+        }
+        wait_landed(bar(kBarFull + s), ph);
       }
+      STREAM_TRACE(4, t_entry);
+      if (a.trace != nullptr) a.trace[blockIdx.x * 16 + 6] = static_cast<unsigned long long>(hi - lo);
+      if (failed) atomicOr(a.status, kStatusTimeout);
     }
     return;
   }
 
-  if (warp == kConsumerWarps + 1) {
-    // ---------------- operand stager ----------------
+  if (warp >= kEpilogueWarp) {
+    // ---------------- operand rows (first epilogue warp) + epilogue ----------------
     if (hi <= lo) return;
-    Cursor cur{tab, cap};
-    const int gc0 = lo / blocks, gc1 = (hi - 1) / blocks;
-    const int K8 = K / 8;  // 8-value pieces per token row
-    for (int gc = gc0; gc <= gc1; ++gc) {
-      const int k = gc - gc0;
-      if (!wait_phase(xempty, (k & 1) ^ 1, abort_flag)) break;
-      const ChunkRef c = cur.at(gc);
-      int my_row = -1;  // lane n < 8: source row of token slot n
-      if (lane < kTok && lane < c.cnt) my_row = GATEUP ? a.sorted_pair[c.s0 + lane] / a.top_k : c.s0 + lane;
-      for (int base = 0; base < kTok * K8; base += 32 * 4) {
-        uint4 raw[4][2];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int pi = base + 32 * u + lane;
-          const int n = pi / K8, kq = pi - n * K8;
-          const int row = __shfl_sync(kFullMask, my_row, n & 7);
-          raw[u][0] = raw[u][1] = make_uint4(0, 0, 0, 0);
-          if (pi < kTok * K8 && row >= 0) {
-            if constexpr (GATEUP) {
-              raw[u][0] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(row) * K + 8 * kq);
-            } else {
-              const uint4* src = reinterpret_cast<const uint4*>(a.h + static_cast<size_t>(row) * K + 8 * kq);
-              raw[u][0] = src[0];
-              raw[u][1] = src[1];
-            }
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int pi = base + 32 * u + lane;
-          if (base + 32 * u >= kTok * K8) break;  // warp-uniform
-          const int n = pi / K8, kq = pi - n * K8;
-          const int G = kq >> 4, t = (kq >> 2) & 3, j = kq & 3;
-          float corr = 0.0f;
-          if constexpr (GATEUP) {
-            xb[(G * 4 + j) * 32 + n * 4 + t] = w4_pack_x(raw[u][0], corr);
-          } else {
-            const float v[8] = {__uint_as_float(raw[u][0].x), __uint_as_float(raw[u][0].y),
-                                __uint_as_float(raw[u][0].z), __uint_as_float(raw[u][0].w),
-                                __uint_as_float(raw[u][1].x), __uint_as_float(raw[u][1].y),
-                                __uint_as_float(raw[u][1].z), __uint_as_float(raw[u][1].w)};
-            uint16_t hb[8], lb[8];
-            float sh = 0.0f, sl = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              split_bf16(v[i], hb[i], lb[i]);
-              sh += bf16_to_f32(hb[i]);
-              sl += bf16_to_f32(lb[i]);
-            }
-            corr = 136.0f * (sh + sl);
-            const int slot = ((G * 4 + j) * 2) * 32 + n * 4 + t;
-            xb[slot] = pack_pairs(pack_bf16x2(hb[0], hb[1]), pack_bf16x2(hb[2], hb[3]), pack_bf16x2(hb[4], hb[5]),
-                                  pack_bf16x2(hb[6], hb[7]));
-            xb[slot + 32] = pack_pairs(pack_bf16x2(lb[0], lb[1]), pack_bf16x2(lb[2], lb[3]),
-                                       pack_bf16x2(lb[4], lb[5]), pack_bf16x2(lb[6], lb[7]));
-          }
-          // the 16 pieces of one (token, group) sit in one half-warp
-#pragma unroll
-          for (int d = 1; d < 16; d <<= 1) corr += __shfl_xor_sync(kFullMask, corr, d);
-          if ((lane & 15) == 0) cb[n * nG + G] = corr;
-        }
+    const int ew = warp - kEpilogueWarp;
+    const uint32_t rowsz = row_bytes<GATEUP>(K);
+    // the activation rows of chunk gc into the raw area, one bulk copy per token
+    auto stage_rows = [&](const ChunkRef& ch) {
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the consumers' reads before the copies
+        ac::mbar_arrive_expect_tx(bar(kBarRaw), static_cast<uint32_t>(ch.cnt) * rowsz);
       }
-      mbar_arrive(xfull);  // release: this lane's stores before the consumers' reads
+      __syncwarp();
+      if (lane < ch.cnt) {
+        const void* src = GATEUP
+            ? static_cast<const void*>(a.x + static_cast<size_t>(a.sorted_pair[ch.s0 + lane] / a.top_k) * K)
+            : static_cast<const void*>(a.h + static_cast<size_t>(ch.s0 + lane) * K);
+        ac::bulk_g2s(ac::smem_u32(raw + static_cast<size_t>(lane) * rowsz), src, rowsz, bar(kBarRaw));
+      }
+    };
+    Cursor cur{tab, cap}, ahead{tab, cap};
+    int gc = lo / blocks, rbk = lo - gc * blocks;
+    const int gc_last = (hi - 1) / blocks;
+    ChunkRef c = cur.at(gc);
+    if (ew == 0) stage_rows(c);
+    int staged = 1, xph = 1;  // chunks whose rows were requested; phase of the next xempty wait
+    bool failed = false;
+    int b = 0, ph = 0;
+    for (int it = lo; it < hi; ++it) {
+      if (!wait_phase(bar(kBarRedFull + b), ph, abort_flag)) {
+        failed = true;
+        break;
+      }
+      // once the consumers have taken a chunk's operands, the next chunk's rows
+      if (ew == 0 && gc + 1 <= gc_last && staged == gc + 1 - lo / blocks) {
+        if (!wait_phase(bar(kBarXEmpty), xph ^ 1, abort_flag)) {
+          failed = true;
+          break;
+        }
+        xph ^= 1;
+        stage_rows(ahead.at(gc + 1));
+        ++staged;
+      }
+      // outputs (token n, row r) of this item, n-major; this warp takes half
+      const float* rp = red + b * kRedFloats;
+      float* ob = a.out + static_cast<size_t>(c.s0) * N + rbk * R;
+      const int rows = GATEUP ? 2 * R : R;  // item rows in the partial-sum buffer
+      const int half = (R * kTok) / kEpilogueWarps;
+#pragma unroll 2
+      for (int o = ew * half + lane; o < (ew + 1) * half; o += 32) {
+        const int n = o / R, r = o - n * R;
+        if (n >= c.cnt) continue;
+        const float* pg = rp + (n * rows + r) * P;
+        float v;
+        if (P % 4 == 0) {
+          float gs = 0.0f;
+          for (int q = 0; q < P; q += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(pg + q);
+            gs = (((gs + f.x) + f.y) + f.z) + f.w;
+          }
+          if constexpr (GATEUP) {
+            const float* pu = pg + R * P;
+            float us = 0.0f;
+            for (int q = 0; q < P; q += 4) {
+              const float4 f = *reinterpret_cast<const float4*>(pu + q);
+              us = (((us + f.x) + f.y) + f.z) + f.w;
+            }
+            v = silu_f32(gs) * us;
+          } else {
+            v = gs;
+          }
+        } else {
+          float gs = 0.0f, us = 0.0f;
+          for (int q = 0; q < P; ++q) {
+            gs += pg[q];
+            if constexpr (GATEUP) us += pg[R * P + q];
+          }
+          v = GATEUP ? silu_f32(gs) * us : gs;
+        }
+        ob[static_cast<size_t>(n) * N + r] = v;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kBarRedEmpty + b));
+      if (++b == kRedBufs) {
+        b = 0;
+        ph ^= 1;
+      }
+      if (++rbk == blocks && it + 1 < hi) {
+        rbk = 0;
+        c = cur.at(++gc);
+      }
     }
+    // the last requested rows land before the CTA may exit
+    if (ew == 0 && lane == 0) wait_landed(bar(kBarRaw), (staged - 1) & 1);
+    if (lane == 0) STREAM_TRACE(5, t_entry);
+    if (failed && lane == 0) atomicOr(a.status, kStatusTimeout);
     return;
   }
 
   // ---------------- consumers ----------------
-  const int part = warp % P, set = warp / P;
+  const int part = warp % P, tl = warp / P;
   const int g = lane >> 2, t = lane & 3;
-  const int grp = a.p0.group;
+  // stage row of this warp's tile row g: gate/up [gate R rows][up R rows]; down [R rows]
+  const int r0 = GATEUP ? (tl & 1) * R + (tl >> 1) * 16 : tl * 16;
+  // per group of this warp: byte offset of the lane's 16 code bytes of row g
+  // within a stage, and the scale element of row g (row g + 8: + 8 rows)
+  uint32_t woff[GPW], soff[GPW];
+  bool gon[GPW];
+  int nv = 0;  // valid groups of this warp: they come first (G = part + gi * P ascending)
+#pragma unroll
+  for (int gi = 0; gi < GPW; ++gi) {
+    const int G = part + gi * P;
+    gon[gi] = G < nG;
+    nv += gon[gi] ? 1 : 0;
+    woff[gi] = static_cast<uint32_t>((r0 + g) * rowb + G * 64 + 16 * t);
+    soff[gi] = static_cast<uint32_t>((r0 + g) * sstride + (G * 128) / a.p0.group);
+  }
+  const uint32_t w8 = static_cast<uint32_t>(8 * rowb), s8 = static_cast<uint32_t>(8 * sstride);
   Cursor cur{tab, cap};
   uint4 bx[GPW][GATEUP ? 4 : 8];
   float cx[GPW][2];
-  int chunk_k = -1;
   bool failed = false;
-  for (int it = lo; it < hi; ++it) {
-    const int k = it - lo;
-    const int gc = it / blocks, rb = it - gc * blocks;
-    const ChunkRef c = cur.at(gc);
-    if (gc - lo / blocks != chunk_k) {  // first item of a chunk: its operands into registers
-      chunk_k = gc - lo / blocks;
-      failed = failed || !wait_phase(xfull, chunk_k & 1, abort_flag);
-      if (!failed) {
-#pragma unroll
-        for (int gi = 0; gi < GPW; ++gi) {
-          const int G = part + gi * P;
-          if (G < nG) {
-#pragma unroll
-            for (int q = 0; q < (GATEUP ? 4 : 8); ++q) {
-              const int j = GATEUP ? q : (q & 3), hl = GATEUP ? 0 : (q >> 2);
-              bx[gi][q] = xb[((G * 4 + j) * (GATEUP ? 1 : 2) + hl) * 32 + lane];
-            }
-            cx[gi][0] = cb[(2 * t) * nG + G];
-            cx[gi][1] = cb[(2 * t + 1) * nG + G];
-          }
-        }
+  int gc = lo / blocks, chunk_end = lo;  // items [.., chunk_end) use the operands in registers
+  int k = 0, s = 0, ph = 0, b = 0, rph = 0, xph = 0;
+  for (int it = lo; it < hi; ++it, ++k) {
+    if (it == chunk_end) {  // first item of a chunk: its operands into registers
+      if (it > lo) ++gc;
+      chunk_end = min(hi, (gc + 1) * blocks);
+      const ChunkRef c = cur.at(gc);
+      if (!wait_phase(bar(kBarRaw), xph, abort_flag)) {
+        failed = true;
+        break;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(xempty);
-    }
-    const int s = k % S;
-    failed = failed || !wait_phase(full0 + 8 * s, (k / S) & 1, abort_flag);
-    float acc[2][4];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-    if (!failed) {
-      const unsigned char* st = stages + static_cast<size_t>(s) * a.stage_bytes;
-      const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + a.code_bytes);
+      xph ^= 1;
+      if (threadIdx.x == 0 && it == lo) STREAM_TRACE(2, t_entry);
+      // lane (g, t) takes token g's 32 activations [32t, 32t + 32) of each of its
+      // groups: operand words in the mma order, and the token's group sum for
+      // the 136 * sum(x) correction (tokens past the chunk's count are zero)
+      const unsigned char* row = raw + static_cast<size_t>(g) * row_bytes<GATEUP>(K);
+      const bool live = g < c.cnt;
 #pragma unroll
       for (int gi = 0; gi < GPW; ++gi) {
         const int G = part + gi * P;
-        if (G < nG) {
-          const int gs = (G * 128) / grp;
+        float sum = 0.0f;
+        if (gon[gi]) {
 #pragma unroll
-          for (int tile = 0; tile < 2; ++tile) {
-            // stage row of tile row g: gate/up [gate R rows][up R rows]; down [R rows]
-            const int r0 = GATEUP ? tile * R + set * 16 : set * 32 + tile * 16;
-            const unsigned char* wp = st + static_cast<size_t>(r0 + g) * rowb + G * 64 + 16 * t;
-            const uint4 wlo = lds128(wp), whi = lds128(wp + 8 * rowb);
-            float d[4];
+          for (int j = 0; j < 4; ++j) {
+            const int k0 = G * 128 + 32 * t + 8 * j;  // first of this word's 8 activations
             if constexpr (GATEUP) {
-              group_x(wlo, whi, bx[gi][0], bx[gi][1], bx[gi][2], bx[gi][3], d);
+              uint4 v = make_uint4(0, 0, 0, 0);
+              if (live) v = lds128(row + 2 * k0);
+              bx[gi][j] = w4_pack_x(v, sum);
             } else {
-              group_hl(wlo, whi, &bx[gi][0], &bx[gi][4], d);
+              uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
+              if (live) {
+                v0 = lds128(row + 4 * k0);
+                v1 = lds128(row + 4 * k0 + 16);
+              }
+              const float f[8] = {__uint_as_float(v0.x), __uint_as_float(v0.y), __uint_as_float(v0.z),
+                                  __uint_as_float(v0.w), __uint_as_float(v1.x), __uint_as_float(v1.y),
+                                  __uint_as_float(v1.z), __uint_as_float(v1.w)};
+              uint16_t hb[8], lb[8];
+              float sh = 0.0f, sl = 0.0f;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                split_bf16(f[i], hb[i], lb[i]);
+                sh += bf16_to_f32(hb[i]);
+                sl += bf16_to_f32(lb[i]);
+              }
+              sum += 136.0f * (sh + sl);
+              bx[gi][j] = pack_pairs(pack_bf16x2(hb[0], hb[1]), pack_bf16x2(hb[2], hb[3]),
+                                     pack_bf16x2(hb[4], hb[5]), pack_bf16x2(hb[6], hb[7]));
+              bx[gi][j + 4] = pack_pairs(pack_bf16x2(lb[0], lb[1]), pack_bf16x2(lb[2], lb[3]),
+                                         pack_bf16x2(lb[4], lb[5]), pack_bf16x2(lb[6], lb[7]));
             }
-            const float s_lo = bf16_to_f32(sc[(r0 + g) * sstride + gs]);
-            const float s_hi = bf16_to_f32(sc[(r0 + g + 8) * sstride + gs]);
-            acc[tile][0] = fmaf(s_lo, d[0] - cx[gi][0], acc[tile][0]);
-            acc[tile][1] = fmaf(s_lo, d[1] - cx[gi][1], acc[tile][1]);
-            acc[tile][2] = fmaf(s_hi, d[2] - cx[gi][0], acc[tile][2]);
-            acc[tile][3] = fmaf(s_hi, d[3] - cx[gi][1], acc[tile][3]);
           }
         }
+        // the 4 lanes of token g hold the group's 4 quarters; the C fragment
+        // columns of lane (g, t) are tokens 2t and 2t + 1
+        sum += __shfl_xor_sync(kFullMask, sum, 1);
+        sum += __shfl_xor_sync(kFullMask, sum, 2);
+        cx[gi][0] = __shfl_sync(kFullMask, sum, (2 * t) * 4);
+        cx[gi][1] = __shfl_sync(kFullMask, sum, (2 * t + 1) * 4);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * s);
-      // partial sums of this K-part: red[buf][part][tile][token][row]
-      float* rp = red + (k & 1) * kRedFloats + (part * (16 / P) + set * 2) * kRedTile;
-#pragma unroll
-      for (int tile = 0; tile < 2; ++tile) {
-        float* r = rp + tile * kRedTile;
-        r[(2 * t) * kRedPitch + g] = acc[tile][0];
-        r[(2 * t + 1) * kRedPitch + g] = acc[tile][1];
-        r[(2 * t) * kRedPitch + g + 8] = acc[tile][2];
-        r[(2 * t + 1) * kRedPitch + g + 8] = acc[tile][3];
-      }
+      if (lane == 0) mbar_arrive(bar(kBarXEmpty));
     }
-    __syncwarp();
-    if (consumers_sync_or(failed || *abort_flag)) {
+    if (!wait_phase(bar(kBarFull + s), ph, abort_flag)) {
       failed = true;
       break;
     }
-    // epilogue: add the P partial sums in part order, write the item's outputs
-    const float* rb_ = red + (k & 1) * kRedFloats;
-    const int tiles_per_part = 16 / P;
-    const int outs = (R / 16) * 128;  // gate/up: 16-row sets; down: 16-row tiles
-    for (int o = threadIdx.x; o < outs; o += kConsumers) {
-      const int tl = o >> 7, n = (o >> 4) & 7, r = o & 15;
-      if (n >= c.cnt) continue;
-      float v;
-      int row;
-      if constexpr (GATEUP) {
-        // tl = set: tiles 2 * set (gate) and 2 * set + 1 (up)
-        float gsum = 0.0f, usum = 0.0f;
-        for (int p = 0; p < P; ++p) {
-          gsum += rb_[(p * tiles_per_part + 2 * tl) * kRedTile + n * kRedPitch + r];
-          usum += rb_[(p * tiles_per_part + 2 * tl + 1) * kRedTile + n * kRedPitch + r];
-        }
-        v = silu_f32(gsum) * usum;
-        row = rb * R + tl * 16 + r;
-      } else {
-        float ysum = 0.0f;
-        for (int p = 0; p < P; ++p) ysum += rb_[(p * tiles_per_part + tl) * kRedTile + n * kRedPitch + r];
-        v = ysum;
-        row = rb * R + tl * 16 + r;  // tile tl = set * 2 + half: rows set * 32 + half * 16
-      }
-      a.out[static_cast<size_t>(c.s0 + n) * N + row] = v;
+    const unsigned char* st = stages + static_cast<size_t>(s) * a.stage_bytes;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + a.code_bytes);
+    const uint32_t eb = bar(kBarEmpty + s);
+    auto release = [eb, lane]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(eb);  // the stage is in registers now
+    };
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (nv == GPW)
+      item_compute<GATEUP, GPW>(st, sc, woff, soff, w8, s8, bx, cx, release, acc);
+    else if (nv > 0)
+      item_compute<GATEUP, 1>(st, sc, woff, soff, w8, s8, bx, cx, release, acc);
+    else
+      release();
+    if (++s == S) {
+      s = 0;
+      ph ^= 1;
+    }
+    // partial sums of this warp: red[buf][warp][token][row]
+    if (!wait_phase(bar(kBarRedEmpty + b), rph ^ 1, abort_flag)) {
+      failed = true;
+      break;
+    }
+    // this warp's partials: red[token][item row][part], item rows of the tile = stage rows r0 + g (+ 8)
+    float* rp = red + b * kRedFloats + (r0 + g) * P + part;
+    const int tok_stride = (GATEUP ? 2 * R : R) * P;
+    rp[(2 * t) * tok_stride] = acc[0];
+    rp[(2 * t + 1) * tok_stride] = acc[1];
+    rp[(2 * t) * tok_stride + 8 * P] = acc[2];
+    rp[(2 * t + 1) * tok_stride + 8 * P] = acc[3];
+    warp_arrive(bar(kBarRedFull + b));
+    if (++b == kRedBufs) {
+      b = 0;
+      rph ^= 1;
     }
   }
-  if (failed && threadIdx.x == 0) atomicOr(a.status, kStatusTimeout);
+  if (threadIdx.x == 0) STREAM_TRACE(3, t_entry);
+  if (failed && lane == 0) atomicOr(a.status, kStatusTimeout);
 }
 
 template <bool GATEUP, int GPW>
@@ -506,17 +663,19 @@ static void* kernel_ptr() {
   return reinterpret_cast<void*>(stream_kernel<GATEUP, GPW>);
 }
 
-// P (K-parts) of a projection: gate/up always 8; down the smallest power of
-// two leaving at most 3 groups per warp.
+// P (K-parts) of a projection.  Gate/up: P = 8, at most 2 groups per
+// consumer warp (16 tiles alternate gate / up, R = 16 rows).  Down: one group
+// per warp (its two-term operand holds twice the registers), the smallest P
+// covering the groups (R = 256 / P rows).
 static int pick_parts(bool gateup, int nG) {
-  if (gateup) return 8;
-  for (int p = 1; p <= 8; p <<= 1)
-    if ((nG + p - 1) / p <= 3) return p;
+  if (gateup) return nG <= 16 ? 8 : 0;
+  for (int p = 1; p <= kConsumerWarps; p <<= 1)
+    if (nG <= p) return p;
   return 0;
 }
 
 struct Plan {
-  Args a;
+  Args a{};  // every pointer null until the launcher sets it (trace stays null for down)
   void* kern = nullptr;
   size_t smem = 0;
 };
@@ -529,10 +688,10 @@ static bool plan(const QuantProj& p0, int max_active, Plan& pl) {
   const int P = pick_parts(GATEUP, nG);
   if (P == 0) return false;
   const int gpw = (nG + P - 1) / P;
-  if (gpw > (GATEUP ? 4 : 3)) return false;
-  const int sets = kConsumerWarps / P;
-  const int R = GATEUP ? 16 * sets : 32 * sets;
-  if (N % R) return false;
+  if (gpw > 2) return false;
+  const int tiles = kConsumerWarps / P;
+  const int R = GATEUP ? 16 * tiles / 2 : 16 * tiles;
+  if (R < 16 || N % R) return false;
   const uint32_t rowb = static_cast<uint32_t>(K / 2);
   const uint32_t code = (GATEUP ? 2u : 1u) * R * rowb;
   const uint32_t scale = (GATEUP ? 2u : 1u) * R * p0.sstride * 2u;
@@ -550,12 +709,10 @@ static bool plan(const QuantProj& p0, int max_active, Plan& pl) {
   a.code_bytes = code;
   a.scale_bytes = scale;
   pl.smem = L.stage + static_cast<size_t>(S) * stage;
-  if constexpr (GATEUP) {
-    pl.kern = gpw == 1 ? kernel_ptr<true, 1>() : gpw == 2 ? kernel_ptr<true, 2>()
-              : gpw == 3 ? kernel_ptr<true, 3>() : kernel_ptr<true, 4>();
-  } else {
-    pl.kern = gpw == 1 ? kernel_ptr<false, 1>() : gpw == 2 ? kernel_ptr<false, 2>() : kernel_ptr<false, 3>();
-  }
+  if constexpr (GATEUP)
+    pl.kern = gpw == 1 ? kernel_ptr<true, 1>() : kernel_ptr<true, 2>();
+  else
+    pl.kern = kernel_ptr<false, 1>();
   return true;
 }
 
@@ -584,7 +741,8 @@ bool stream_eligible(int bits, const QuantProj& gate, const QuantProj& up, const
 }
 
 int launch_stream_gateup(const uint16_t* x, const RouteTables& rt, int top_k, int max_active, const QuantProj& gate,
-                         const QuantProj& up, float* h, int* status, int num_sms, cudaStream_t st) {
+                         const QuantProj& up, float* h, int* status, unsigned long long* trace, int num_sms,
+                         cudaStream_t st) {
   sm::Plan pl;
   if (!sm::plan<true>(gate, max_active, pl)) return -1;
   sm::Args& a = pl.a;
@@ -598,6 +756,7 @@ int launch_stream_gateup(const uint16_t* x, const RouteTables& rt, int top_k, in
   a.p1 = up;
   a.out = h;
   a.status = status;
+  a.trace = trace;
   return sm::launch(pl, num_sms, st);
 }
 

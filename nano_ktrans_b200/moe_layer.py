@@ -169,6 +169,18 @@ class MoeLayer:
                                           _ptr(out_weights), _stream_handle(stream)), self._h, "moe_forward")
         return out
 
+    def forward_host(self, x: torch.Tensor, router_logits: torch.Tensor, out: torch.Tensor, stream=None) -> None:
+        """forward() on host tensors (bf16, contiguous, ideally pinned): copies in,
+        runs the step and copies the result into `out`, all enqueued on the
+        stream — `out` is valid after the stream is synchronised."""
+        for name, tsr, cols in (("x", x, self.hidden_size), ("router_logits", router_logits, self.num_experts),
+                                ("out", out, self.hidden_size)):
+            if (tsr.device.type != "cpu" or tsr.dtype is not torch.bfloat16 or tsr.dim() != 2
+                    or tsr.shape[1] != cols or tsr.shape[0] != x.shape[0] or not tsr.is_contiguous()):
+                raise ValueError(f"{name} must be a contiguous bf16 host tensor [T, {cols}]")
+        _lib.check(_lib.lib().moe_forward_host(self._h, x.data_ptr(), router_logits.data_ptr(), int(x.shape[0]),
+                                               out.data_ptr(), _stream_handle(stream)), self._h, "moe_forward_host")
+
     def _check_router(self, router_weight: torch.Tensor) -> None:
         if (not self._on_device(router_weight) or router_weight.dtype != torch.bfloat16
                 or tuple(router_weight.shape) != (self.num_experts, self.hidden_size)
