@@ -185,6 +185,18 @@ MOE_DEV float chunk_dot(uint4 wv, const float4* xs4, int stride4) {
 // (0,4) (1,5) (2,6) (3,7) of the word shifted right by 0, 4, 8 and 12 bits.
 // ---------------------------------------------------------------------------
 
+// (x & mask) | bits in one LOP3 (LUT 0xEA = (a & b) | c).  Written out because
+// the compiler does not always fuse the AND and the OR, and the nibble unpacks
+// of the W4 kernels are bound by this ALU work.
+MOE_DEV uint32_t and_or(uint32_t x, uint32_t mask, uint32_t bits) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(mask), "r"(bits));
+  return r;
+}
+
+// Nibble pair of x at bits 0-3 and 16-19 as two exact bf16 values 128 + q.
+MOE_DEV uint32_t nib_bf16(uint32_t x) { return and_or(x, 0x000F000Fu, 0x43004300u); }
+
 MOE_DEV uint32_t pack_bf16x2(uint16_t lo, uint16_t hi) { return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16); }
 
 // raw = 8 consecutive bf16 activations (x0..x7, two per 32-bit word, low half
@@ -212,17 +224,16 @@ MOE_DEV void fma2_f32_bf16(float& a0, float& a1, uint32_t x, uint32_t v) {
 // (xq[q * stride4], q = 0..3), minus the chunk correction; unscaled by the
 // group scale.
 MOE_DEV float w4_chunk_dot_bf16(uint4 wv, const uint4* xq, int stride4, float corr) {
-  constexpr uint32_t M = 0x43004300u;
   float a0 = 0.0f, a1 = 0.0f;
   const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const uint32_t ww = w[q];
     const uint4 xv = xq[q * stride4];
-    fma2_f32_bf16(a0, a1, xv.x, (ww & 0x000F000Fu) | M);
-    fma2_f32_bf16(a0, a1, xv.y, ((ww >> 4) & 0x000F000Fu) | M);
-    fma2_f32_bf16(a0, a1, xv.z, ((ww >> 8) & 0x000F000Fu) | M);
-    fma2_f32_bf16(a0, a1, xv.w, ((ww >> 12) & 0x000F000Fu) | M);
+    fma2_f32_bf16(a0, a1, xv.x, nib_bf16(ww));
+    fma2_f32_bf16(a0, a1, xv.y, nib_bf16(ww >> 4));
+    fma2_f32_bf16(a0, a1, xv.z, nib_bf16(ww >> 8));
+    fma2_f32_bf16(a0, a1, xv.w, nib_bf16(ww >> 12));
   }
   return (a0 + a1) - corr;
 }

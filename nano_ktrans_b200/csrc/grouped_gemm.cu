@@ -168,7 +168,7 @@ MOE_DEV void dequant16(uint4 c, __half2 sc, uint4* out) {
       uint32_t v[4];
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        const uint32_t m = ((w[q] >> (4 * s)) & 0x000F000Fu) | 0x64006400u;  // fp16 (1024 + q_s, 1024 + q_{s+4})
+        const uint32_t m = and_or(w[q] >> (4 * s), 0x000F000Fu, 0x64006400u);  // fp16 (1024 + q_s, 1024 + q_{s+4})
         __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&m), bias);    // q - 8, exact
         h = __hmul2(h, sc);                                                  // (q - 8) * s, exact
         v[s] = *reinterpret_cast<uint32_t*>(&h);

@@ -40,7 +40,6 @@ MOE_DEV void mma16816_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
 // few hundred cycles of latency, so the 8 steps go to 4 independent
 // accumulators (chains of 2), added in a fixed order at the end.
 MOE_DEV void w4_group_mma(uint4 wlo, uint4 whi, const uint4* xr, float (&d)[4]) {
-  constexpr uint32_t M = 0x43004300u, N = 0x000F000Fu;
   const uint32_t u[4] = {wlo.x, wlo.y, wlo.z, wlo.w};
   const uint32_t v[4] = {whi.x, whi.y, whi.z, whi.w};
   float e[4][4];
@@ -49,10 +48,10 @@ MOE_DEV void w4_group_mma(uint4 wlo, uint4 whi, const uint4* xr, float (&d)[4]) 
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const uint4 x = xr[q];
-    mma16816_bf16(e[(2 * q) & 3], (u[q] & N) | M, (v[q] & N) | M, ((u[q] >> 4) & N) | M, ((v[q] >> 4) & N) | M,
+    mma16816_bf16(e[(2 * q) & 3], nib_bf16(u[q]), nib_bf16(v[q]), nib_bf16(u[q] >> 4), nib_bf16(v[q] >> 4),
                   x.x, x.y);
-    mma16816_bf16(e[(2 * q + 1) & 3], ((u[q] >> 8) & N) | M, ((v[q] >> 8) & N) | M, ((u[q] >> 12) & N) | M,
-                  ((v[q] >> 12) & N) | M, x.z, x.w);
+    mma16816_bf16(e[(2 * q + 1) & 3], nib_bf16(u[q] >> 8), nib_bf16(v[q] >> 8), nib_bf16(u[q] >> 12),
+                  nib_bf16(v[q] >> 12), x.z, x.w);
   }
 #pragma unroll
   for (int r = 0; r < 4; ++r) d[r] = (e[0][r] + e[1][r]) + (e[2][r] + e[3][r]);

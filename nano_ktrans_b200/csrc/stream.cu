@@ -198,12 +198,6 @@ MOE_DEV uint4 pack_pairs(uint32_t p01, uint32_t p23, uint32_t p45, uint32_t p67)
 struct AWords {
   uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
 };
-// (x & 0x000F000F) | 0x43004300 as one LOP3 (LUT 0xEA = (a & b) | c).
-MOE_DEV uint32_t nib_bf16(uint32_t x) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "n"(0x000F000F), "r"(0x43004300u));
-  return r;
-}
 MOE_DEV AWords unpack_a(uint32_t u, uint32_t v) {
   AWords w;
   w.a0 = nib_bf16(u);
