@@ -661,7 +661,16 @@ def main():
         line["e2e"] = {"value": args.e2e_steps * args.batch * world / (e_ms / 1e3), "unit": "tokens/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                        "api": "moe_forward_host per step (C ABI via MoeLayer.forward_host): pinned host x and "
-                              "logits in, bf16 output back to pinned host memory"}
+                              "logits read by the device through their mapped addresses, bf16 output stored by "
+                              "the step's last kernel into pinned host memory"}
+        for lay in layers:
+            lay.set_host_io(0)
+        d_ms, _, _ = run_e2e_host(layers, x, logits, args.e2e_steps)
+        for lay in layers:
+            lay.set_host_io(2)
+        line["e2e"]["copy_engine"] = {
+            "value": args.e2e_steps * args.batch * world / (max_over_ranks(d_ms) / 1e3), "unit": "tokens/s",
+            "api": "moe_forward_host with copy-engine copies in and out"}
         t_ms, _, _ = run_e2e(layers, x, logits, args.e2e_steps)
         t_ms = max_over_ranks(t_ms)
         line["e2e"]["moe_layer_forward"] = {

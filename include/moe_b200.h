@@ -144,10 +144,11 @@ int moe_forward(void* handle, const uint16_t* x_dev, const uint16_t* logits_dev,
                 uint16_t* topk_weights_dev, void* stream);
 
 /* moe_forward with HOST buffers: x_host [T, H] and logits_host [T, E] bf16
- * are copied into the handle's workspace, the step runs, and the bf16 output
- * is copied back into out_host [T, H] — all enqueued on `stream`; the output
- * is valid once the stream reaches that point.  The host buffers should be
- * page-locked (pageable memory makes the copies synchronous). */
+ * are moved into the handle's workspace, the step runs, and the bf16 output
+ * lands in out_host [T, H] — all enqueued on `stream`; the output is valid
+ * once the stream reaches that point.  Page-locked buffers are read (and, with
+ * MOE_OPT_HOST_IO 2, written) by the kernels through their mapped addresses;
+ * pageable buffers go through copy-engine copies (synchronous ones). */
 int moe_forward_host(void* handle, const uint16_t* x_host, const uint16_t* logits_host,
                      int32_t num_tokens, uint16_t* out_host, void* stream);
 
@@ -251,7 +252,13 @@ enum moe_option {
    * expert's rows read once per call, applied to up to 8 of its tokens at a
    * time) when the layer is W4 with inter, hidden and group_size multiples of
    * 128; 0 = the CUDA-core matvec kernels. */
-  MOE_OPT_STREAM = 5
+  MOE_OPT_STREAM = 5,
+  /* How moe_forward_host moves page-locked host buffers: 0 = copy-engine
+   * copies in and out; 1 = a kernel reads the inputs from mapped host memory,
+   * the output is copied back; 2 (default) = as 1, and the step's last kernel
+   * stores the output straight into host memory.  Pageable buffers always take
+   * the copy engine (each call asks the driver which kind every pointer is). */
+  MOE_OPT_HOST_IO = 6
 };
 
 /* Copy the phase stamps of the last traced single-launch decode step, 16 per

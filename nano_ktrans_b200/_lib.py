@@ -15,7 +15,7 @@ HEADER_PATH = os.path.join(os.path.dirname(PKG_DIR), "include", "moe_b200.h")
 
 MOE_OK, MOE_EINVAL, MOE_ECUDA, MOE_ENOWEIGHTS, MOE_ERANGE, MOE_EDEVICE = range(6)
 K_ROUTE, K_PERMUTE, K_GATEUP, K_DOWN, K_COMBINE, K_DECODE_FUSED = range(1, 7)
-OPT_DECODE_FUSED, OPT_TRACE, OPT_GEMM, OPT_GEMM_TILE, OPT_STREAM = 1, 2, 3, 4, 5
+OPT_DECODE_FUSED, OPT_TRACE, OPT_GEMM, OPT_GEMM_TILE, OPT_STREAM, OPT_HOST_IO = 1, 2, 3, 4, 5, 6
 
 _DESC_FIELDS = ("num_experts", "top_k", "hidden_size", "inter_size", "bits", "group_size",
                 "router_use_softmax", "normalize_topk_prob", "max_tokens", "shared_inter")

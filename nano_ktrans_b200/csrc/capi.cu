@@ -50,6 +50,7 @@ struct Handle {
   int gemm_mode = 1;            // 0 never, 1 by batch size, 2 whenever the shape allows
   int gemm_tile = 0;            // token-tile width of the GEMM launches: 0 by batch, else 16/32/64/128
   int stream_mode = 1;          // 1: weight-streaming kernels where eligible, 0: matvec kernels
+  int host_io = 2;              // moe_forward_host: 0 copies, 1 device reads the inputs, 2 also stores the output
   bool gemm_maps = false;       // tensor maps encoded (shape supported, driver entry point found)
   // activation maps, one per token-tile width 16 << i
   alignas(64) unsigned char tm_x[moe::kGemmTileWidths][128];  // fp16 [max_pairs][H] over ybuf (x in pair order)
@@ -602,13 +603,29 @@ int moe_forward_host(void* handle, const uint16_t* x_host, const uint16_t* logit
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t xb = sizeof(uint16_t) * static_cast<size_t>(T) * h->d.hidden_size;
   const size_t lb = sizeof(uint16_t) * static_cast<size_t>(T) * h->d.num_experts;
-  if (cudaMemcpyAsync(h->x_stage, x_host, xb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-      cudaMemcpyAsync(h->logits_tmp, logits_host, lb, cudaMemcpyHostToDevice, st) != cudaSuccess)
+  // Page-locked host buffers are mapped into the device's address space: the
+  // inputs are then read by one small kernel (no copy-engine round trips) and,
+  // with host_io 2, the output is stored straight into host memory by the
+  // step's last kernel.  Pageable buffers always take the copy engine.
+  // every call asks the driver what each pointer is: a kernel may only touch
+  // memory that is page-locked and mapped right now
+  const bool in_mapped = h->host_io > 0 && xb % 16 == 0 && lb % 16 == 0 && moe::host_mapped(x_host) &&
+                         moe::host_mapped(logits_host);
+  const bool out_mapped = h->host_io > 1 && moe::host_mapped(out_host);
+  int launches = 0;
+  if (in_mapped) {
+    moe::launch_stage_in(x_host, xb, logits_host, lb, h->x_stage, h->logits_tmp, st);
+    launches = 1;
+  } else if (cudaMemcpyAsync(h->x_stage, x_host, xb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+             cudaMemcpyAsync(h->logits_tmp, logits_host, lb, cudaMemcpyHostToDevice, st) != cudaSuccess) {
     return fail(h, MOE_ECUDA, "moe_forward_host: input copy failed: %s", cudaGetErrorString(cudaGetLastError()));
-  if (int rc = moe_forward(handle, h->x_stage, h->logits_tmp, T, h->out_stage, nullptr, nullptr, stream)) return rc;
-  if (cudaMemcpyAsync(out_host, h->out_stage, xb, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+  }
+  uint16_t* dst = out_mapped ? out_host : h->out_stage;
+  if (int rc = moe_forward(handle, h->x_stage, h->logits_tmp, T, dst, nullptr, nullptr, stream)) return rc;
+  h->last_launches += launches;
+  if (!out_mapped && cudaMemcpyAsync(out_host, h->out_stage, xb, cudaMemcpyDeviceToHost, st) != cudaSuccess)
     return fail(h, MOE_ECUDA, "moe_forward_host: output copy failed: %s", cudaGetErrorString(cudaGetLastError()));
-  return MOE_OK;
+  return check_launch(h, "moe_forward_host");
 }
 
 int moe_router_logits(void* handle, const uint16_t* x_dev, const uint16_t* router_w_dev, int32_t T,
@@ -766,6 +783,10 @@ int moe_set_option(void* handle, int32_t option, int32_t value) {
       if (value != 0 && value != 16 && value != 32 && value != 64 && value != 128)
         return fail(h, MOE_EINVAL, "moe_set_option(gemm tile): value must be 0, 16, 32, 64 or 128");
       h->gemm_tile = value;
+      return MOE_OK;
+    case MOE_OPT_HOST_IO:
+      if (value < 0 || value > 2) return fail(h, MOE_EINVAL, "moe_set_option(host io): value must be 0, 1 or 2");
+      h->host_io = value;
       return MOE_OK;
     case MOE_OPT_STREAM:
       if (value < 0 || value > 1) return fail(h, MOE_EINVAL, "moe_set_option(stream): value must be 0 or 1");

@@ -115,6 +115,11 @@ struct DecodeT1Params {
 // Dynamic shared-memory opt-in + one-CTA-per-SM check, done once per (kernel,
 // device) and new maximum size (launch_util.cu).
 bool ensure_dynamic_smem(const void* kern, size_t smem, int threads);
+// Page-locked, device-mapped host memory (readable by kernels through the same pointer).
+bool host_mapped(const void* p);
+// xd <- x, ld <- l (byte counts multiples of 16) by a kernel reading mapped host memory.
+void launch_stage_in(const void* x, size_t xbytes, const void* l, size_t lbytes, void* xd, void* ld,
+                     cudaStream_t st);
 
 bool decode_t1_eligible(const DecodeT1Params& p);
 // 1 = launched; negative = not launched.

@@ -254,6 +254,12 @@ class MoeLayer:
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_STREAM, int(bool(enabled))), self._h,
                    "moe_set_option")
 
+    def set_host_io(self, mode: int) -> None:
+        """forward_host with page-locked buffers: 0 copy-engine copies, 1 a kernel
+        reads the inputs from mapped host memory, 2 (default) also the output is
+        stored straight into host memory."""
+        _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_HOST_IO, int(mode)), self._h, "moe_set_option")
+
     def set_gemm_tile(self, width: int) -> None:
         """Token-tile width of the grouped GEMM: 0 chooses by batch, else 16, 32, 64 or 128."""
         _lib.check(_lib.lib().moe_set_option(self._h, _lib.OPT_GEMM_TILE, int(width)), self._h, "moe_set_option")

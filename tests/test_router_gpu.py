@@ -90,18 +90,27 @@ def test_forward_x_matches_oracle(tokens, cuda_device):
     layer.close()
 
 
-def test_forward_host_matches_forward(cuda_device):
-    """moe_forward_host (host buffers in and out) gives the bits of forward()."""
+@pytest.mark.parametrize("host_io", [0, 1, 2])
+def test_forward_host_matches_forward(host_io, cuda_device):
+    """moe_forward_host (host buffers in and out) gives the bits of forward(), for
+    copy-engine transfers, kernel reads of mapped host memory (and direct stores
+    of the output), pinned and pageable buffers, on the single-token kernel and
+    the multi-kernel path."""
     cfg = dict(experts=16, top_k=4, hidden=256, inter=256, use_softmax=True, renormalize=True)
     for tokens in (1, 6):
         layer, _ = _layer(cfg, cuda_device, tokens, 800 + tokens)
+        layer.set_host_io(host_io)
         g = torch.Generator(device=cuda_device).manual_seed(tokens)
         x = torch.randn(tokens, 256, generator=g, device=cuda_device).to(torch.bfloat16)
         lg = (torch.randn(tokens, 16, generator=g, device=cuda_device)).to(torch.bfloat16)
-        want = layer.forward(x, lg)
-        xh, lh = x.cpu().pin_memory(), lg.cpu().pin_memory()
-        oh = torch.empty_like(xh).pin_memory()
-        layer.forward_host(xh, lh, oh)
-        torch.cuda.synchronize()
-        assert torch.equal(oh.view(torch.int16), want.cpu().view(torch.int16))
+        want = layer.forward(x, lg).cpu()
+        for pinned in (True, False):
+            xh, lh = x.cpu(), lg.cpu()
+            oh = torch.empty_like(xh)
+            if pinned:
+                xh, lh, oh = xh.pin_memory(), lh.pin_memory(), oh.pin_memory()
+            layer.forward_host(xh, lh, oh)
+            torch.cuda.synchronize()
+            assert torch.equal(oh.view(torch.int16), want.view(torch.int16)), (tokens, pinned)
+        assert layer.read_status() == 0
         layer.close()
