@@ -62,15 +62,22 @@
 namespace moe {
 namespace sm {
 
-constexpr int kConsumerWarps = 16;
-constexpr int kProducerWarp = 16, kEpilogueWarp = 17, kEpilogueWarps = 2;
-constexpr int kThreads = (kEpilogueWarp + kEpilogueWarps) * 32;
+// Warp roles per projection: gate/up 16 consumer warps, 1 producer, 2 epilogue
+// warps; down (whose items are small and whose every output sums P partials)
+// 12 consumer warps and 4 epilogue warps.
+template <bool GATEUP> struct Roles {
+  static constexpr int kConsumerWarps = GATEUP ? 16 : 12;
+  static constexpr int kProducerWarp = kConsumerWarps;
+  static constexpr int kEpilogueWarp = kConsumerWarps + 1;
+  static constexpr int kEpilogueWarps = GATEUP ? 2 : 4;
+  static constexpr int kThreads = (kEpilogueWarp + kEpilogueWarps) * 32;
+};
 constexpr int kTok = 8;  // tokens per chunk: the mma's N
 constexpr int kMaxStages = 8;
 constexpr int kRedBufs = 3;
 // A partial-sum buffer holds red[token][item row][K-part]: the P partials of
-// one output are adjacent (vector loads in the epilogue).  Item rows x P is
-// 256 in every configuration (gate/up: 2R rows, R = 128 / P; down: R = 256 / P).
+// one output are adjacent (vector loads in the epilogue).  Item rows x P is at
+// most 256 (gate/up: 2R rows, R = 128 / P; down: R = 16 * consumers / P rows).
 constexpr int kRedRowParts = 256;
 constexpr int kRedFloats = kTok * kRedRowParts;
 constexpr int kSmemLimit = 227 * 1024;
@@ -283,7 +290,10 @@ MOE_DEV void item_compute(const unsigned char* st, const uint16_t* sc, const uin
 }
 
 template <bool GATEUP, int GPW>
-__global__ void __launch_bounds__(kThreads, 1) stream_kernel(Args a) {
+__global__ void __launch_bounds__(Roles<GATEUP>::kThreads, 1) stream_kernel(Args a) {
+  constexpr int kConsumerWarps = Roles<GATEUP>::kConsumerWarps, kProducerWarp = Roles<GATEUP>::kProducerWarp,
+                kEpilogueWarp = Roles<GATEUP>::kEpilogueWarp, kEpilogueWarps = Roles<GATEUP>::kEpilogueWarps,
+                kThreads = Roles<GATEUP>::kThreads;
   extern __shared__ __align__(128) unsigned char smem[];
   const int K = a.p0.k, N = a.p0.n;
   const int nG = K / 128;
@@ -475,18 +485,19 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(Args a) {
         if (n >= c.cnt) continue;
         const float* pg = rp + (n * rows + r) * P;
         float v;
-        if (P % 4 == 0) {
+        if (P % 2 == 0) {
+          // partials of one output, in part order, by pairs (P even)
           float gs = 0.0f;
-          for (int q = 0; q < P; q += 4) {
-            const float4 f = *reinterpret_cast<const float4*>(pg + q);
-            gs = (((gs + f.x) + f.y) + f.z) + f.w;
+          for (int q = 0; q < P; q += 2) {
+            const float2 f = *reinterpret_cast<const float2*>(pg + q);
+            gs = (gs + f.x) + f.y;
           }
           if constexpr (GATEUP) {
             const float* pu = pg + R * P;
             float us = 0.0f;
-            for (int q = 0; q < P; q += 4) {
-              const float4 f = *reinterpret_cast<const float4*>(pu + q);
-              us = (((us + f.x) + f.y) + f.z) + f.w;
+            for (int q = 0; q < P; q += 2) {
+              const float2 f = *reinterpret_cast<const float2*>(pu + q);
+              us = (us + f.x) + f.y;
             }
             v = silu_f32(gs) * us;
           } else {
@@ -657,14 +668,17 @@ static void* kernel_ptr() {
   return reinterpret_cast<void*>(stream_kernel<GATEUP, GPW>);
 }
 
-// P (K-parts) of a projection.  Gate/up: P = 8, at most 2 groups per
-// consumer warp (16 tiles alternate gate / up, R = 16 rows).  Down: one group
-// per warp (its two-term operand holds twice the registers), the smallest P
-// covering the groups (R = 256 / P rows).
-static int pick_parts(bool gateup, int nG) {
-  if (gateup) return nG <= 16 ? 8 : 0;
-  for (int p = 1; p <= kConsumerWarps; p <<= 1)
-    if (nG <= p) return p;
+// P (K-parts) of a projection; P divides the consumer warp count and the
+// item's rows R = 16 * tiles (gate/up: tiles alternate gate and up rows, so
+// R = 8 * tiles) must divide N.  Gate/up: P = 8, at most 2 groups per warp.
+// Down: one group per warp (its two-term operand holds twice the registers),
+// the smallest P covering the groups.
+template <bool GATEUP>
+static int pick_parts(int nG, int N) {
+  constexpr int C = Roles<GATEUP>::kConsumerWarps;
+  if (GATEUP) return nG <= 16 ? 8 : 0;
+  for (int p = 1; p <= C; ++p)
+    if (C % p == 0 && nG <= p && N % (16 * (C / p)) == 0) return p;
   return 0;
 }
 
@@ -672,6 +686,7 @@ struct Plan {
   Args a{};  // every pointer null until the launcher sets it (trace stays null for down)
   void* kern = nullptr;
   size_t smem = 0;
+  int threads = 0;
 };
 
 template <bool GATEUP>
@@ -679,11 +694,11 @@ static bool plan(const QuantProj& p0, int max_active, Plan& pl) {
   const int K = p0.k, N = p0.n;
   if (K % 128 || p0.group % 128 || K % p0.group) return false;
   const int nG = K / 128;
-  const int P = pick_parts(GATEUP, nG);
+  const int P = pick_parts<GATEUP>(nG, N);
   if (P == 0) return false;
   const int gpw = (nG + P - 1) / P;
   if (gpw > 2) return false;
-  const int tiles = kConsumerWarps / P;
+  const int tiles = Roles<GATEUP>::kConsumerWarps / P;
   const int R = GATEUP ? 16 * tiles / 2 : 16 * tiles;
   if (R < 16 || N % R) return false;
   const uint32_t rowb = static_cast<uint32_t>(K / 2);
@@ -703,6 +718,7 @@ static bool plan(const QuantProj& p0, int max_active, Plan& pl) {
   a.code_bytes = code;
   a.scale_bytes = scale;
   pl.smem = L.stage + static_cast<size_t>(S) * stage;
+  pl.threads = Roles<GATEUP>::kThreads;
   if constexpr (GATEUP)
     pl.kern = gpw == 1 ? kernel_ptr<true, 1>() : kernel_ptr<true, 2>();
   else
@@ -711,10 +727,10 @@ static bool plan(const QuantProj& p0, int max_active, Plan& pl) {
 }
 
 static int launch(Plan& pl, int num_sms, cudaStream_t st) {
-  if (!ensure_dynamic_smem(pl.kern, pl.smem, kThreads)) return -1;
+  if (!ensure_dynamic_smem(pl.kern, pl.smem, pl.threads)) return -1;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(num_sms);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(pl.threads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
