@@ -75,8 +75,8 @@ template <bool GATEUP> struct Roles {
 constexpr int kTok = 8;  // tokens per chunk: the mma's N
 constexpr int kMaxStages = 8;
 constexpr int kRedBufs = 3;
-// A partial-sum buffer holds red[token][item row][K-part]: the P partials of
-// one output are adjacent (vector loads in the epilogue).  Item rows x P is at
+// A partial-sum buffer holds red[token][K-part][item row]: the epilogue's lanes
+// read consecutive rows of one part (no bank conflicts).  Item rows x P is at
 // most 256 (gate/up: 2R rows, R = 128 / P; down: R = 16 * consumers / P rows).
 constexpr int kRedRowParts = 256;
 constexpr int kRedFloats = kTok * kRedRowParts;
@@ -483,34 +483,16 @@ __global__ void __launch_bounds__(Roles<GATEUP>::kThreads, 1) stream_kernel(Args
       for (int o = ew * half + lane; o < (ew + 1) * half; o += 32) {
         const int n = o / R, r = o - n * R;
         if (n >= c.cnt) continue;
-        const float* pg = rp + (n * rows + r) * P;
-        float v;
-        if (P % 2 == 0) {
-          // partials of one output, in part order, by pairs (P even)
-          float gs = 0.0f;
-          for (int q = 0; q < P; q += 2) {
-            const float2 f = *reinterpret_cast<const float2*>(pg + q);
-            gs = (gs + f.x) + f.y;
-          }
-          if constexpr (GATEUP) {
-            const float* pu = pg + R * P;
-            float us = 0.0f;
-            for (int q = 0; q < P; q += 2) {
-              const float2 f = *reinterpret_cast<const float2*>(pu + q);
-              us = (us + f.x) + f.y;
-            }
-            v = silu_f32(gs) * us;
-          } else {
-            v = gs;
-          }
-        } else {
-          float gs = 0.0f, us = 0.0f;
-          for (int q = 0; q < P; ++q) {
-            gs += pg[q];
-            if constexpr (GATEUP) us += pg[R * P + q];
-          }
-          v = GATEUP ? silu_f32(gs) * us : gs;
+        // partials red[n][q][row] for q = 0..P-1, added in part order; consecutive
+        // lanes read consecutive rows (no bank conflicts)
+        const float* pg = rp + n * P * rows + r;
+        float gs = 0.0f, us = 0.0f;
+#pragma unroll 4
+        for (int q = 0; q < P; ++q) {
+          gs += pg[q * rows];
+          if constexpr (GATEUP) us += pg[q * rows + R];
         }
+        const float v = GATEUP ? silu_f32(gs) * us : gs;
         ob[static_cast<size_t>(n) * N + r] = v;
       }
       __syncwarp();
@@ -646,13 +628,13 @@ __global__ void __launch_bounds__(Roles<GATEUP>::kThreads, 1) stream_kernel(Args
       failed = true;
       break;
     }
-    // this warp's partials: red[token][item row][part], item rows of the tile = stage rows r0 + g (+ 8)
-    float* rp = red + b * kRedFloats + (r0 + g) * P + part;
-    const int tok_stride = (GATEUP ? 2 * R : R) * P;
-    rp[(2 * t) * tok_stride] = acc[0];
-    rp[(2 * t + 1) * tok_stride] = acc[1];
-    rp[(2 * t) * tok_stride + 8 * P] = acc[2];
-    rp[(2 * t + 1) * tok_stride + 8 * P] = acc[3];
+    // this warp's partials: red[token][part][item row], item rows of the tile = stage rows r0 + g (+ 8)
+    const int rows = GATEUP ? 2 * R : R;
+    float* rp = red + b * kRedFloats + part * rows + r0 + g;
+    rp[(2 * t) * P * rows] = acc[0];
+    rp[(2 * t + 1) * P * rows] = acc[1];
+    rp[(2 * t) * P * rows + 8] = acc[2];
+    rp[(2 * t + 1) * P * rows + 8] = acc[3];
     warp_arrive(bar(kBarRedFull + b));
     if (++b == kRedBufs) {
       b = 0;
