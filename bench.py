@@ -588,7 +588,10 @@ def main():
         if torch.distributed.is_initialized():
             torch.distributed.destroy_process_group()
         return
-    uniq = [make_unique_layer(gen, dev) for _ in range(min(UNIQUE_LAYERS, args.layers))]
+    # expert weights are the same on every rank (the expert-parallel leg shards one
+    # model across the ranks); inputs differ per rank
+    wgen = torch.Generator(device=dev).manual_seed(args.seed)
+    uniq = [make_unique_layer(wgen, dev) for _ in range(min(UNIQUE_LAYERS, args.layers))]
     lws = [uniq[i] if i < len(uniq) else clone_layer(uniq[i % len(uniq)]) for i in range(args.layers)]
     max_b = max([args.batch] + [int(b) for b in args.sweep.split(",") if b])
     layers = [MoeLayer(lw, top_k=CFG["top_k"], router_use_softmax=True, normalize_topk_prob=True, max_tokens=max_b)
@@ -1294,25 +1297,30 @@ def ep_parity(layers, uniq, xp, lp, xd, ld, world, rank, max_tokens, n_check: in
     else:
         comm = TorchDistComm()
         ep = layers[:n_check]
-    tokens = torch.zeros(2, dtype=torch.float64, device=xp[0].device)  # checked tokens, mismatching tokens
+    # checked tokens, mismatching tokens, mismatching elements, max |difference| (summed / maxed over ranks)
+    tokens = torch.zeros(3, dtype=torch.float64, device=xp[0].device)
+    worst = torch.zeros(1, dtype=torch.float64, device=xp[0].device)
     for i in range(n_check):
         ref = MoeLayer(uniq[i % len(uniq)], top_k=k, router_use_softmax=True, normalize_topk_prob=True,
                        max_tokens=max_tokens)
         for xs, lg in ((xp, lp), (xd, ld)):
             got = ep[i].forward(xs[i], lg[i], comm)[0].clone()
             want = ref.forward(xs[i], lg[i]).clone()
-            bad = (got.view(torch.int16) != want.view(torch.int16)).any(dim=1)
+            diff = got.view(torch.int16) != want.view(torch.int16)
             tokens[0] += got.shape[0]
-            tokens[1] += bad.sum()
+            tokens[1] += diff.any(dim=1).sum()
+            tokens[2] += diff.sum()
+            worst = torch.maximum(worst, (got.float() - want.float()).abs().max().double().reshape(1))
         torch.cuda.synchronize()
         ref.close()
     for lay in own:
         lay.close()
     if torch.distributed.is_initialized():
         torch.distributed.all_reduce(tokens)
-    return {"checked_tokens": int(tokens[0]), "mismatches": int(tokens[1]), "layers": n_check,
-            "batches": "prefill and decode", "compare": "bf16 bit pattern vs MoeLayer.forward on the same GPU",
-            "ranks": world}
+        torch.distributed.all_reduce(worst, op=torch.distributed.ReduceOp.MAX)
+    return {"checked_tokens": int(tokens[0]), "mismatches": int(tokens[1]), "mismatching_elements": int(tokens[2]),
+            "max_abs_diff": float(worst[0]), "layers": n_check, "batches": "prefill and decode",
+            "compare": "bf16 bit pattern vs MoeLayer.forward on the same GPU", "ranks": world}
 
 
 def read_traffic(kernel: str, batch: int):
