@@ -24,32 +24,33 @@
 // chunk-major, and each CTA of the persistent grid takes one contiguous range
 // of items, so a CTA sees one or two chunks and streams their rows in order.
 //
-// Warp roles, one CTA per SM:
-//   warps 0-15  consumers.  The 16 warps are P K-parts x (16 / P) 16-row
-//               tiles: warp w computes tile w / P of the item over the
-//               128-code groups p, p + P, ... of K-part p = w % P.  Gate/up
-//               tiles alternate gate and up rows (R = 8 * 16 / P); down tiles
-//               are consecutive rows (R = 16 * 16 / P).  A warp keeps its
-//               K-part's B fragments in registers for the whole chunk.
-//   warp 16     producer: one lane issues, per item, the bulk copies of its
+// Warp roles, one CTA per SM (gate/up: C = 16 consumer warps, E = 2 epilogue
+// warps; down: C = 12, E = 4 — see Roles):
+//   warps 0..C-1  consumers.  P K-parts x (C / P) 16-row tiles: warp w
+//               computes tile w / P of the item over the 128-code groups p,
+//               p + P, ... of K-part p = w % P.  Gate/up tiles alternate gate
+//               and up rows (R = 8 * C / P); down tiles are consecutive rows
+//               (R = 16 * C / P).  A warp keeps its K-part's B fragments in
+//               registers for the whole chunk.
+//   warp C      producer: one lane issues, per item, the bulk copies of its
 //               code rows and scale rows into the next ring stage.
-//   warp 17     rows + epilogue.  Bulk-copies each chunk's activation rows
-//               (gate/up: the bf16 x rows of its tokens; down: the fp32 h
-//               rows) into a shared-memory area once the consumers have taken
-//               the previous chunk's (each consumer warp builds its B fragments
-//               and per-group corrections from those rows once per chunk;
-//               down splits h into its bf16 hi + lo terms).  Per item, adds
-//               the P partial sums of each output in part order (results do
-//               not depend on timing), applies SiLU(g) * u for gate/up, and
-//               stores the outputs.
+//   warps C+1.. rows + epilogue.  The first of them bulk-copies each chunk's
+//               activation rows (gate/up: the bf16 x rows of its tokens; down:
+//               the fp32 h rows) into a shared-memory area once the consumers
+//               have taken the previous chunk's (each consumer warp builds its
+//               B fragments and per-group corrections from those rows once per
+//               chunk; down splits h into its bf16 hi + lo terms).  Per item,
+//               the E warps each take part of the outputs: add the P partial
+//               sums in part order (results do not depend on timing), apply
+//               SiLU(g) * u for gate/up, and store.
 // The consumers pass partial sums to the epilogue through a ring of
 // shared-memory buffers, so no consumer waits for another.
 //
 // Every wait is bounded (2 s of %globaltimer; while waiting, a warp is
 // suspended on the mbarrier rather than spinning).  A wait that runs out sets
 // the CTA's abort flag and the status word (kStatusTimeout); every role then
-// leaves, the producer and the stager after their copies in flight have landed
-// (bounded as well).
+// leaves, the producer and the row-copying warp after their copies in flight
+// have landed (bounded as well).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -81,7 +82,7 @@ constexpr int kRedBufs = 3;
 constexpr int kRedRowParts = 256;
 constexpr int kRedFloats = kTok * kRedRowParts;
 constexpr int kSmemLimit = 227 * 1024;
-// mbarriers: full[kMaxStages], empty[kMaxStages], red_full[kRedBufs], red_empty[kRedBufs], xfull, xempty, raw
+// mbarriers: full[kMaxStages], empty[kMaxStages], red_full[kRedBufs], red_empty[kRedBufs], xempty, raw
 constexpr int kBarFull = 0, kBarEmpty = kMaxStages, kBarRedFull = 2 * kMaxStages,
               kBarRedEmpty = 2 * kMaxStages + kRedBufs, kBarXEmpty = 2 * kMaxStages + 2 * kRedBufs,
               kBarRaw = kBarXEmpty + 1, kNumBars = kBarXEmpty + 2;
@@ -98,7 +99,7 @@ struct Args {
   QuantProj p0, p1;  // gate, up | down
   float* out;        // gate/up: SiLU(g)*u [pairs][N]; down: y [pairs][N]
   int* status;
-  unsigned long long* trace;  // optional [G][16] %globaltimer stamps (gate/up launch), see kTrace*
+  unsigned long long* trace;  // optional [G][16] %globaltimer stamps (gate/up launch), see STREAM_TRACE
   int parts;         // P
   int rows;          // R: output rows per item
   int stages;
