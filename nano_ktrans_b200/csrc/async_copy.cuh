@@ -81,5 +81,37 @@ MOE_DEV bool grid_sync_bounded(unsigned long long* bar, int* ok_smem) {
   return *ok_smem != 0;
 }
 
+// The same barrier with the arrival off the critical path.  grid_epoch_read
+// reads the counter once, after griddepcontrol.wait and before this CTA
+// arrives: every CTA of the launch then sees a value in [n * G, n * G + G - 1]
+// (the previous launch's G arrivals are complete, this launch's are not all in)
+// and grid_sync_epoch derives the same target (n + 1) * G from it.  The
+// arrival is a posted release-add, with no round trip for its return value.
+// Issue the read after the CTA's first copies: its result is only needed at
+// the barrier.
+MOE_DEV unsigned long long grid_epoch_read(const unsigned long long* bar) {
+  cuda::atomic_ref<const unsigned long long, cuda::thread_scope_device> count(*bar);
+  return count.load(cuda::memory_order_relaxed);
+}
+
+MOE_DEV bool grid_sync_epoch(unsigned long long* bar, unsigned long long seen, int* ok_smem) {
+  __syncthreads();  // the CTA's writes are ordered before thread 0's release (cumulativity)
+  if (threadIdx.x == 0) {
+    const unsigned long long g = gridDim.x, target = (seen / g + 1) * g;
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
+    cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> count(*bar);
+    int ok = 1;
+    for (uint32_t i = 0; count.load(cuda::memory_order_acquire) < target; ++i) {
+      if (i > kSpinLimit) {
+        ok = 0;
+        break;
+      }
+    }
+    *ok_smem = ok;
+  }
+  __syncthreads();
+  return *ok_smem != 0;
+}
+
 }  // namespace ac
 }  // namespace moe

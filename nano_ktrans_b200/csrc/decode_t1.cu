@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const long long t_entry = clock64();
   T1_TRACE(0);
+  unsigned long long bar_seen = 0;  // thread 0: the grid-barrier counter before this CTA arrives
   if (tid == 0) {
     // the input barrier first, so the input copies leave before the other inits
     const uint32_t b0 = ac::smem_u32(&bars[0]);
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
     for (int i = 1; i < 2 + kMaxChunks; ++i) ac::mbar_init(ac::smem_u32(&bars[i]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tb.abort = 0;
+    bar_seen = ac::grid_epoch_read(a.bar);
   }
   __syncthreads();
   const bool in_ok = __all_sync(kFullMask, ac::mbar_wait_bounded(ac::smem_u32(&bars[0]), 0u));
@@ -330,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_t1_kernel(Args a) {
   T1_TRACE(7);
 
   // ---- 4. grid barrier, stage h ----------------------------------------------------------------
-  const bool passed = ac::grid_sync_bounded(a.bar, &grid_ok);
+  const bool passed = ac::grid_sync_epoch(a.bar, bar_seen, &grid_ok);
   if (!passed && tid == 0) fail();
   T1_TRACE(8);
   // Stage h as bf16 (hi, lo) operand words: word w = 4c + q (8 activations,
