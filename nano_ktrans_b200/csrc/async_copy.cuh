@@ -56,32 +56,9 @@ MOE_DEV unsigned long long global_ns() {
   return t;
 }
 
-// Grid-wide barrier for a cooperative launch.  The 64-bit arrival counter
-// only grows: a CTA's arrival returns n, its launch's barrier is complete
-// when the counter reaches (n / G + 1) * G.  No reset, no second atomic.
-// Returns false if the wait hit its iteration limit.  Only thread 0 fences and
-// polls: the block barrier on either side orders the other threads' accesses.
-MOE_DEV bool grid_sync_bounded(unsigned long long* bar, int* ok_smem) {
-  __syncthreads();  // the CTA's writes are ordered before thread 0's fence (cumulativity)
-  if (threadIdx.x == 0) {
-    __threadfence();
-    cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> count(*bar);
-    const unsigned long long g = gridDim.x;
-    const unsigned long long target = (count.fetch_add(1ull, cuda::memory_order_acq_rel) / g + 1) * g;
-    int ok = 1;
-    for (uint32_t i = 0; count.load(cuda::memory_order_acquire) < target; ++i) {
-      if (i > kSpinLimit) {
-        ok = 0;
-        break;
-      }
-    }
-    *ok_smem = ok;
-  }
-  __syncthreads();
-  return *ok_smem != 0;
-}
-
-// The same barrier with the arrival off the critical path.  grid_epoch_read
+// Grid-wide barrier for a cooperative launch.  The 64-bit arrival counter only
+// grows: launch n's barrier is complete when the counter reaches (n + 1) * G.
+// The arrival is kept off the critical path.  grid_epoch_read
 // reads the counter once, after griddepcontrol.wait and before this CTA
 // arrives: every CTA of the launch then sees a value in [n * G, n * G + G - 1]
 // (the previous launch's G arrivals are complete, this launch's are not all in)

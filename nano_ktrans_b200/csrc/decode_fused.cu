@@ -96,7 +96,6 @@ struct Tables {
 // mbarrier, bulk-copy and grid-barrier primitives: async_copy.cuh
 using ac::bulk_g2s;
 using ac::global_ns;
-using ac::grid_sync_bounded;
 using ac::mbar_init;
 using ac::mbar_try_wait;
 using ac::mbar_wait_bounded;
@@ -136,10 +135,12 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
   __shared__ int grid_ok;
 
   MOE_TRACE(0);
+  unsigned long long bar_seen = 0;  // thread 0: the grid-barrier counter before this CTA arrives
   if (tid == 0) {
     for (int s = 0; s <= kFStages; ++s) mbar_init(smem_u32(&bars[s]), 1);  // ring slots + phase-C region
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tb.abort = 0;
+    bar_seen = ac::grid_epoch_read(a.bar);
   }
   for (int i = tid; i < T * kFRowsC; i += kFThreads) out_acc[i] = 0.0f;
 
@@ -318,7 +319,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
     if (d.kind == 1 && !synced) {
       // phase B -> C: grid barrier, then stage every pair's h (pre-scaled)
       MOE_TRACE(2);
-      const bool passed = grid_sync_bounded(a.bar, &grid_ok);
+      const bool passed = ac::grid_sync_epoch(a.bar, bar_seen, &grid_ok);
       MOE_TRACE(3);
       if (!passed && tid == 0) {
         atomicOr(a.status, kStatusTimeout);
@@ -507,7 +508,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
     if (tid == 0 && !tb.abort && issued < nring && issued == j + kFStages) issue(issued++);
   }
   if (!synced) {
-    if (!grid_sync_bounded(a.bar, &grid_ok) && tid == 0) atomicOr(a.status, kStatusTimeout);
+    if (!ac::grid_sync_epoch(a.bar, bar_seen, &grid_ok) && tid == 0) atomicOr(a.status, kStatusTimeout);
   }
   // abort path: let copies that were issued but never waited on land before
   // the CTA's shared memory is released (bounded)
