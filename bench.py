@@ -65,6 +65,12 @@ def parse_args():
                     help="config 5: global prefill,decode token counts of the 48-layer expert-parallel stack "
                          "('' = skip)")
     ap.add_argument("--ep-steps", type=int, default=3)
+    ap.add_argument("--ep-exchange", default="peer", choices=("peer", "nccl"),
+                    help="expert-parallel exchanges: the library's kernels over peer memory (CUDA IPC), or two "
+                         "NCCL all_to_all_single calls per layer with a host read of the split sizes")
+    ap.add_argument("--ep-graph", type=int, default=1,
+                    help="with the peer exchange, replay the 48-layer step as one CUDA graph (1) or launch it "
+                         "eagerly (0)")
     ap.add_argument("--m32", type=int, default=200,
                     help="steps of the dense bf16 stacked-bmm batch-1 comparator (0 = skip)")
     ap.add_argument("--no-c1", action="store_true", help="skip the config-1 (W8 per-channel, batch 1) decode line")
@@ -1164,10 +1170,12 @@ def prefill_block(args, dev, rank):
 def run_ep(args, world, rank, dev, uniq, lws):
     """Config 5: the 48-layer Qwen3-shaped stack (W4 g128, Zipf(1.2) routing)
     with each layer's 128 experts split over the ranks (frequency-balanced
-    placement, NCCL all-to-all dispatch and combine); global prefill and
-    decode batches split evenly over the ranks.  One GPU runs the same
-    layers through the single-GPU path.  Times are CUDA events around a
-    pass over all 48 layers (max over ranks)."""
+    placement; exchanges over peer memory, or NCCL all-to-alls with
+    --ep-exchange nccl); global prefill and decode batches split evenly over
+    the ranks.  One GPU runs the same layers through the single-GPU path.
+    Times are CUDA events around a pass over all 48 layers (max over ranks);
+    with --ep-graph (default) the pass is one CUDA graph replay at every N
+    (the NCCL exchange, which reads split sizes on the host, runs eagerly)."""
     import torch
 
     from nano_ktrans_b200.expert_parallel import EpMoeLayer, TorchDistComm, plan_placement, shard_layer
@@ -1193,6 +1201,7 @@ def run_ep(args, world, rank, dev, uniq, lws):
     res = {"placement": "frequency-balanced (prefill batch routing counts, all ranks)", "world": world,
            "zipf": {"alpha": 1.2, "beta": beta, "fitted_alpha": fit_alpha}}
 
+    exchange = None
     if world == 1:
         layers = [MoeLayer(lw, top_k=k, router_use_softmax=True, normalize_topk_prob=True, max_tokens=tp)
                   for lw in lws]
@@ -1200,9 +1209,15 @@ def run_ep(args, world, rank, dev, uniq, lws):
         def step(xs, lg):
             for lay, x, g in zip(layers, xs, lg):
                 lay.forward(x, g)
-        res["path"] = "single GPU: moe_forward per layer (all experts local)"
+        res["path"] = "single GPU: moe_forward per layer (all experts local)" + (
+            "; the 48-layer step replayed as one CUDA graph" if args.ep_graph else "")
     else:
         comm = TorchDistComm()
+        if args.ep_exchange == "peer":
+            from nano_ktrans_b200.expert_parallel import PeerExchange
+
+            exchange = PeerExchange(rank, world, max_tokens=max(tp, td), top_k=k, hidden=H, num_experts=E, device=dev)
+            exchange.connect_ipc()
         probe = EpMoeLayer(shard_layer(uniq[0], plan_placement(E, world), rank, world), num_experts=E, top_k=k,
                            slot_of_expert=plan_placement(E, world), rank=rank, world=world, max_tokens=tp)
         layers = []
@@ -1218,29 +1233,48 @@ def run_ep(args, world, rank, dev, uniq, lws):
                 loads[int(slot[e]) // epr] += float(freq[e])
             max_ratio = max(max_ratio, max(loads) / (sum(loads) / world))
             layers.append(EpMoeLayer(shard_layer(uniq[i % len(uniq)], slot, rank, world), num_experts=E, top_k=k,
-                                     slot_of_expert=slot, rank=rank, world=world, max_tokens=max(tp, td)))
+                                     slot_of_expert=slot, rank=rank, world=world, max_tokens=max(tp, td),
+                                     exchange=exchange))
         probe.close()
         res["max_rank_load_over_mean"] = max_ratio
 
         def step(xs, lg):
+            # every rank's token count is at most ceil(global / world): the peer step's work bound
+            bound = -(-(n_prefill if xs is xp else n_decode) // world)
             for lay, x, g in zip(layers, xs, lg):
-                lay.forward(x, g, comm)
-        res["path"] = ("expert parallel: moe_ep_dispatch -> NCCL all_to_all -> moe_rows_forward -> all_to_all "
-                       "-> moe_ep_combine")
+                lay.forward(x, g, comm, tokens_per_rank=bound)
+        if exchange is not None:
+            res["path"] = ("expert parallel over peer memory: moe_route -> moe_ep_peer_publish -> "
+                           "moe_ep_peer_experts (token rows read from every rank's region over NVLink, outputs "
+                           "stored into the token's rank's region) -> moe_ep_peer_combine; epoch flags, no host "
+                           "read, no collective" + ("; the 48-layer step replayed as one CUDA graph"
+                                                    if args.ep_graph else ""))
+        else:
+            res["path"] = ("expert parallel: moe_ep_dispatch -> NCCL all_to_all -> moe_rows_forward -> "
+                           "all_to_all -> moe_ep_combine")
 
     def timed(xs, lg, steps):
         step(xs, lg)  # warm-up pass
         torch.cuda.synchronize()
+        run = lambda: step(xs, lg)  # noqa: E731
+        graph = None
+        if (exchange is not None or world == 1) and args.ep_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step(xs, lg)
+            run = graph.replay
         if torch.distributed.is_initialized():
             torch.distributed.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            step(xs, lg)
+            run()
         e1.record()
         torch.cuda.synchronize()
-        return max_over_ranks(e0.elapsed_time(e1) / steps)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        del graph
+        return ms
 
     flops_layer = 2.0 * n_prefill * k * 3 * H * CFG["inter"]
     ms = timed(xp, lp, args.ep_steps)
@@ -1249,10 +1283,14 @@ def run_ep(args, world, rank, dev, uniq, lws):
     ms = timed(xd, ld, 3 * args.ep_steps)
     res["decode"] = {"global_tokens": n_decode, "ms_per_48_layers": ms, "tokens_per_s": n_decode / (ms / 1e3)}
     res["ep_parity"] = ep_parity(layers, uniq, xp, lp, xd, ld, world, rank, tp)
+    if exchange is not None:
+        res["ep_parity"]["exchange_status"] = exchange.read_status()
     if world == 1 and not args.no_cpu_baseline and args.cpu_seconds > 0:
         res["cpu_baseline"] = ep_cpu_baseline(layers[0], lws[0], xp[0], lp[0], xd[0], ld[0], L, args.cpu_seconds)
     for lay in layers:
         lay.close()
+    if exchange is not None:
+        exchange.close(barrier=torch.distributed.barrier)
     torch.cuda.empty_cache()
     return res
 

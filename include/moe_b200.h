@@ -200,6 +200,74 @@ int moe_rows_forward(void* handle, const uint16_t* x_rows_dev, const int64_t* ro
 int moe_ep_combine(void* handle, const int64_t* topk_ids_dev, const uint16_t* topk_weights_dev, int32_t num_tokens,
                    const float* returned_rows_dev, uint16_t* out_dev, void* stream);
 
+/* ---- Expert parallelism over peer memory (no counterpart in the reference) ----
+ * The same split of the routed experts over `world` ranks (one process per
+ * GPU, every GPU reachable from every other over NVLink / NVSwitch), with
+ * the exchanges done by this library's kernels through each rank's
+ * "region": one device allocation of the same layout on every rank, opened
+ * by the others through CUDA IPC.  Nothing in a step reads device memory
+ * back to the host, so a whole multi-layer step can be captured in a CUDA
+ * graph; ranks hand over with epoch flags in the regions (bounded waits:
+ * a wait that runs out sets MOE_EP_STATUS_TIMEOUT in the group's status word
+ * and every later wait of the group returns at once until the word is read).
+ *
+ * Region of a rank: flags, its published token count, slots [max_tokens][top_k]
+ * (int32 expert slot of each routed pair), x [max_tokens][hidden] (bf16 token
+ * rows) and y [max_tokens][top_k][hidden] (fp32 expert output of each pair,
+ * written by the pair's owner).
+ *
+ * One step on every rank, in this order on one stream:
+ *   1. moe_ep_peer_publish: copies x and the slots of the routed ids
+ *      (slot_of_expert as in moe_ep_dispatch) into the region; signals
+ *      "ready" to every rank.
+ *   2. moe_ep_peer_experts (expert_handle: the rank's experts_per_rank experts,
+ *      top_k = the layer's, max_tokens >= world * group max_tokens): waits for
+ *      every rank's "ready"; gathers every rank's token rows, selects the
+ *      pairs whose slot this rank owns, runs them through its experts and
+ *      stores each fp32 output row into the token's rank's y at (token, slot
+ *      index); signals "done" to every rank.  tokens_per_rank (0: the group's
+ *      max_tokens) bounds every rank's token count in this step and sizes the
+ *      work (a rank above it is clamped and MOE_EP_STATUS_OVERFLOW set);
+ *      pairs_hint (the pairs this rank expects, e.g. its own T * top_k) only
+ *      picks the kernels.
+ *   3. moe_ep_peer_combine: waits for every rank's "done"; out[t] =
+ *      bf16(sum over slots j in ascending expert order of w[t][j] * y[t][j]),
+ *      fp32, the single-GPU combine's arithmetic and order.
+ * A pair's output does not depend on which other pairs share its kernels, so
+ * the result is bit-identical to moe_experts_forward on one GPU whenever the
+ * expert kernels chosen are the same.
+ * Lifetime: a rank may destroy its group only after every rank has finished
+ * its last step (synchronise, then a host barrier). */
+#define MOE_EP_STATUS_BAD_ID 1
+#define MOE_EP_STATUS_TIMEOUT 2
+#define MOE_EP_STATUS_OVERFLOW 4
+#define MOE_EP_IPC_HANDLE_BYTES 64
+int moe_ep_group_create(int32_t rank, int32_t world, int32_t max_tokens, int32_t top_k, int32_t hidden_size,
+                        int32_t num_experts, void** group, char* err, size_t err_len);
+/* Unmap the other ranks' regions (every rank first finishes its last step and
+ * meets the others at a host barrier), then free this rank's region once every
+ * rank has unmapped it (a second barrier). */
+int moe_ep_group_close_peers(void* group);
+int moe_ep_group_destroy(void* group);
+/* CUDA IPC handle of this rank's region (MOE_EP_IPC_HANDLE_BYTES bytes). */
+int moe_ep_group_ipc_handle(void* group, void* handle_out);
+/* Open `peer`'s region from its IPC handle (peer != own rank). */
+int moe_ep_group_open_peer(void* group, int32_t peer, const void* ipc_handle);
+/* Emulated ranks in one process on one device: this rank's region pointer,
+ * and another group's region given directly. */
+int moe_ep_group_region(void* group, void** region_dev);
+int moe_ep_group_set_peer(void* group, int32_t peer, void* region_dev);
+int moe_ep_peer_publish(void* group, const uint16_t* x_dev, const int64_t* topk_ids_dev, int32_t num_tokens,
+                        const int32_t* slot_of_expert_dev, void* stream);
+int moe_ep_peer_experts(void* group, void* expert_handle, int32_t tokens_per_rank, int32_t pairs_hint,
+                        void* stream);
+int moe_ep_peer_combine(void* group, const int64_t* topk_ids_dev, const uint16_t* topk_weights_dev,
+                        int32_t num_tokens, uint16_t* out_dev, void* stream);
+/* Copy the group's status word to *status and clear it (synchronises `stream`). */
+int moe_ep_group_read_status(void* group, int32_t* status, void* stream);
+/* Last error message of the group's calls, as moe_last_error. */
+int moe_ep_group_last_error(void* group, char* buf, size_t len);
+
 /* Dequantize rows [row0, row0+nrows) of projection `proj` (0 gate, 1 up,
  * 2 down, 3..5 shared gate/up/down) of expert `expert` into fp32 [nrows, K],
  * with the same unpack code the matvec kernels use. */

@@ -7,8 +7,9 @@ Public API (mirrors the reference's names):
 * ``CudaMoEBackend`` — the ``"cuda"`` expert backend
 * ``HybridMoE`` — the MoE layer using it
 * ``MoeLayer`` — direct access to the C-ABI handle (route / experts / fused forward)
-* ``EpMoeLayer``, ``plan_placement``, ``shard_layer``, ``TorchDistComm`` — expert
-  parallelism over the ranks of a process group
+* ``EpMoeLayer``, ``plan_placement``, ``shard_layer``, ``TorchDistComm``,
+  ``PeerExchange`` — expert parallelism over the ranks of a process group (NCCL
+  all-to-alls, or the library's kernels over peer memory)
 """
 from .offload_backend import ExpertOffloadBackend, normalize_offload_backend_name
 from .weights import GPTQLinearWeight, LayerWeights, quantize_symmetric, stack_layer
@@ -16,7 +17,7 @@ from .weights import GPTQLinearWeight, LayerWeights, quantize_symmetric, stack_l
 __all__ = [
     "ExpertOffloadBackend", "normalize_offload_backend_name", "GPTQLinearWeight", "LayerWeights",
     "quantize_symmetric", "stack_layer", "CudaMoEBackend", "HybridMoE", "MoeLayer",
-    "EpMoeLayer", "plan_placement", "shard_layer", "TorchDistComm",
+    "EpMoeLayer", "plan_placement", "shard_layer", "TorchDistComm", "PeerExchange",
 ]
 
 
@@ -30,7 +31,7 @@ def __getattr__(name):
     if name == "MoeLayer":
         from .moe_layer import MoeLayer
         return MoeLayer
-    if name in ("EpMoeLayer", "plan_placement", "shard_layer", "TorchDistComm"):
+    if name in ("EpMoeLayer", "plan_placement", "shard_layer", "TorchDistComm", "PeerExchange"):
         from . import expert_parallel
         return getattr(expert_parallel, name)
     raise AttributeError(name)

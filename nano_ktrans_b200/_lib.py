@@ -67,7 +67,22 @@ SIGNATURES = {
     "moe_ep_dispatch": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
     "moe_rows_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
     "moe_ep_combine": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp]),
+    "moe_ep_group_create": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_vp), _cp, _sz]),
+    "moe_ep_group_ipc_handle": (_i32, [_vp, _vp]),
+    "moe_ep_group_open_peer": (_i32, [_vp, _i32, _vp]),
+    "moe_ep_group_region": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "moe_ep_group_set_peer": (_i32, [_vp, _i32, _vp]),
+    "moe_ep_peer_publish": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "moe_ep_peer_experts": (_i32, [_vp, _vp, _i32, _i32, _vp]),
+    "moe_ep_peer_combine": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "moe_ep_group_read_status": (_i32, [_vp, ctypes.POINTER(_i32), _vp]),
+    "moe_ep_group_last_error": (_i32, [_vp, _cp, _sz]),
+    "moe_ep_group_close_peers": (_i32, [_vp]),
+    "moe_ep_group_destroy": (_i32, [_vp]),
 }
+
+EP_IPC_HANDLE_BYTES = 64
+EP_STATUS_BAD_ID, EP_STATUS_TIMEOUT, EP_STATUS_OVERFLOW = 1, 2, 4
 
 _lib = None
 
@@ -100,6 +115,17 @@ def last_error(handle) -> str:
     buf = ctypes.create_string_buffer(1024)
     lib().moe_last_error(handle, buf, len(buf))
     return buf.value.decode(errors="replace")
+
+
+def group_error(group) -> str:
+    buf = ctypes.create_string_buffer(1024)
+    lib().moe_ep_group_last_error(group, buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check_group(rc: int, group, what: str) -> None:
+    if rc != MOE_OK:
+        raise MoeError(rc, f"{what}: {group_error(group) if group else ''}")
 
 
 def check(rc: int, handle=None, what: str = "") -> None:

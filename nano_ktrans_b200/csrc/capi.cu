@@ -16,6 +16,7 @@
 
 #include "../../include/moe_b200.h"
 #include "common.cuh"
+#include "ep_peer.h"
 #include "kernels.h"
 
 namespace {
@@ -414,21 +415,32 @@ static bool try_decode_fused(Handle* h, const uint16_t* x, const uint16_t* logit
 // weighted combine into `out`; with rows_out set, k is 1 (each "token" is one
 // (token, expert) row), the shared expert is skipped and the unweighted fp32
 // expert output of row r goes to rows_out[r].
+// Output of the expert-parallel peer step (moe_ep_peer_experts): each pair's
+// fp32 row goes to its token's rank's region instead of a local combine.
+struct PeerScatter {
+  const moe::PeerView* view;
+  const unsigned long long* epoch;
+  unsigned int* counter;
+  int bound;       // tokens per rank in the step: T = world * bound
+  int pairs_hint;  // pairs expected among the T*k slots: picks the kernels
+};
+
 static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, const uint16_t* wts, int T,
                            const uint8_t* mask, bool add_shared, uint16_t* out, cudaStream_t st, int launches,
-                           float* rows_out = nullptr) {
+                           float* rows_out = nullptr, const PeerScatter* peer = nullptr) {
   const moe_layer_desc& d = h->d;
   const int E = d.num_experts, H = d.hidden_size, I = d.inter_size;
   const int k = rows_out ? 1 : d.top_k;
-  if (rows_out) add_shared = false;
-  if (launches == 0 && !rows_out &&
+  if (rows_out || peer) add_shared = false;
+  if (launches == 0 && !rows_out && !peer &&
       try_decode_fused(h, x, nullptr, ids, wts, nullptr, nullptr, T, mask, add_shared, out, st))
     return check_launch(h, "moe_experts_forward");
   prof_mark(h, MOE_K_PERMUTE, false, st);
-  moe::launch_permute(ids, T, k, E, mask, h->rt, st);
+  moe::launch_permute(ids, T, k, E, mask, h->rt, st, peer != nullptr);
   prof_mark(h, MOE_K_PERMUTE, true, st);
   ++launches;
   const int max_active = std::min(E, T * k);
+  const int pairs = peer ? std::max(1, std::min(peer->pairs_hint, T * k)) : T * k;  // for the kernel choice
   const QuantProj gate = make_proj(h, h->w.gate_q_dev, h->w.gate_s_dev, I, H);
   const QuantProj up = make_proj(h, h->w.up_q_dev, h->w.up_s_dev, I, H);
   const QuantProj down = make_proj(h, h->w.down_q_dev, h->w.down_s_dev, H, I);
@@ -437,8 +449,8 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
   const bool shared_gemm = add_shared && d.shared_inter > 0 && h->shared_gemm_maps && h->gemm_mode != 0 &&
                            (h->gemm_mode == 2 || T >= 16);
   const bool stream_ok = h->stream_mode && moe::stream_eligible(d.bits, gate, up, down, max_active);
-  const bool routed_gemm = use_gemm(h, T * k, stream_ok);
-  const int bn = h->gemm_tile ? h->gemm_tile : pick_bn(T * k, E);
+  const bool routed_gemm = use_gemm(h, pairs, stream_ok);
+  const int bn = h->gemm_tile ? h->gemm_tile : pick_bn(pairs, E);
   const int sbn = h->gemm_tile ? h->gemm_tile : pick_bn(T, 1);
   if (routed_gemm || shared_gemm) {
     moe::launch_tile_table(h->rt, h->tile_off, shared_gemm ? h->sh_tables : nullptr, T, bn, sbn, st);
@@ -542,14 +554,17 @@ static int experts_forward(Handle* h, const uint16_t* x, const int64_t* ids, con
     sy = h->sh_y;
   }
   prof_mark(h, MOE_K_COMBINE, false, st);
-  if (rows_out)
+  if (peer)
+    moe::launch_ep_peer_scatter(*peer->view, h->rt.pair_pos, T * k, peer->bound, h->ybuf, peer->epoch,
+                                peer->counter, h->num_sms, st);
+  else if (rows_out)
     moe::launch_scatter_rows(h->rt.pair_pos, T, H, h->ybuf, rows_out, h->num_sms, st);
   else
     moe::launch_combine(ids, wts, h->rt, T, k, H, h->ybuf, sg, sy, out, st);
   prof_mark(h, MOE_K_COMBINE, true, st);
   ++launches;
   h->last_launches = launches;
-  return check_launch(h, rows_out ? "moe_rows_forward" : "moe_experts_forward");
+  return check_launch(h, peer ? "moe_ep_peer_experts" : rows_out ? "moe_rows_forward" : "moe_experts_forward");
 }
 
 static int check_forward_args(Handle* h, const void* x, const void* out, int T) {
@@ -706,6 +721,38 @@ int moe_rows_forward(void* handle, const uint16_t* x_rows_dev, const int64_t* ro
     return fail(h, MOE_EINVAL, "moe_rows_forward: null device pointer");
   return experts_forward(h, x_rows_dev, row_expert_dev, nullptr, n, nullptr, false, nullptr,
                          static_cast<cudaStream_t>(stream), 0, y_rows_dev);
+}
+
+int moe_ep_peer_experts(void* group, void* expert_handle, int32_t tokens_per_rank, int32_t pairs_hint,
+                        void* stream) {
+  auto* g = static_cast<moe::PeerGroup*>(group);
+  Handle* h = static_cast<Handle*>(expert_handle);
+  if (g == nullptr || h == nullptr) return MOE_EINVAL;
+  const moe::PeerView& v = g->v;
+  auto gerr = [&](int code, const char* msg) {
+    g->err = std::string("moe_ep_peer_experts: ") + msg;
+    return code;
+  };
+  if (g->phase != 1) return gerr(MOE_EINVAL, "moe_ep_peer_publish has not run for this step");
+  if (!h->has_weights) return gerr(MOE_ENOWEIGHTS, "the expert handle has no weights");
+  if (h->device != g->device) return gerr(MOE_EINVAL, "the expert handle lives on another device");
+  if (h->d.num_experts != v.experts_per_rank || h->d.top_k != v.top_k || h->d.hidden_size != v.hidden)
+    return gerr(MOE_EINVAL, "the expert handle must hold num_experts / world experts with the group's top_k and hidden");
+  const int bound = tokens_per_rank > 0 ? tokens_per_rank : v.max_tokens;
+  if (bound > v.max_tokens) return gerr(MOE_ERANGE, "tokens_per_rank above the group's max_tokens");
+  if (bound < g->published_tokens) return gerr(MOE_ERANGE, "tokens_per_rank below this rank's published tokens");
+  const int T_all = v.world * bound;
+  if (h->d.max_tokens < T_all) return gerr(MOE_ERANGE, "the expert handle's max_tokens is below world * tokens_per_rank");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaGetLastError();
+  moe::launch_ep_peer_collect(v, g->epoch, bound, g->x_all, g->ids_all, g->num_sms, st);
+  const PeerScatter ps{&g->v, g->epoch, g->counters + 1, bound, pairs_hint};
+  if (int rc = experts_forward(h, g->x_all, g->ids_all, nullptr, T_all, nullptr, false, nullptr, st, 1, nullptr, &ps)) {
+    g->err = "moe_ep_peer_experts: " + h->err;
+    return rc;
+  }
+  g->phase = 2;
+  return MOE_OK;
 }
 
 int moe_ep_combine(void* handle, const int64_t* ids_dev, const uint16_t* w_dev, int32_t T, const float* rows_dev,

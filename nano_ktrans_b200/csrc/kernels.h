@@ -36,8 +36,11 @@ bool router_shape_ok(int E, int H, const void* x, const void* wr);
 void launch_router_logits(const uint16_t* x, const uint16_t* wr, int T, int E, int H, uint16_t* logits,
                           cudaStream_t st);
 
+// Stable counting sort of the T*top_k pairs by expert (route tables).  Ids
+// outside [0, E) are excluded and flagged in the status word, except negative
+// ids when skip_negative (pairs that belong to no local expert).
 void launch_permute(const int64_t* ids, int T, int top_k, int E, const uint8_t* offload_mask,
-                    const RouteTables& rt, cudaStream_t st);
+                    const RouteTables& rt, cudaStream_t st, bool skip_negative = false);
 
 // gate/up projection + SiLU(gate)*up for every (expert, token) pair:
 // h[s][n] for sorted positions s.  When identity_tokens > 0 the routing

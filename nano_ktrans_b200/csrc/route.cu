@@ -161,7 +161,8 @@ __device__ int block_incl_scan(int v, int* warp_sums) {
 }
 
 __global__ void __launch_bounds__(1024) permute_kernel(const int64_t* __restrict__ ids, int P, int E,
-                                                       const uint8_t* __restrict__ mask, RouteTables rt) {
+                                                       const uint8_t* __restrict__ mask, int skip_negative,
+                                                       RouteTables rt) {
   extern __shared__ int sm[];
   int* cnt = sm;                // [E]
   int* run = cnt + E;           // [E]
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int64_t* __restrict
   for (int p = tid; p < P; p += blockDim.x) {
     const int64_t e = ids[p];
     if (e < 0 || e >= E) {
-      bad = true;
+      bad |= e >= E || !skip_negative;  // negative ids mark unrouted pairs when skip_negative
       continue;
     }
     if (mask == nullptr || mask[e]) atomicAdd(&cnt[e], 1);
@@ -241,14 +242,14 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int64_t* __restrict
 }
 
 void launch_permute(const int64_t* ids, int T, int top_k, int E, const uint8_t* offload_mask, const RouteTables& rt,
-                    cudaStream_t st) {
+                    cudaStream_t st, bool skip_negative) {
   const size_t smem = sizeof(int) * (3 * static_cast<size_t>(E) + 1 + 32 + 32 * static_cast<size_t>(E));
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     configured = true;
   }
-  permute_kernel<<<1, 1024, smem, st>>>(ids, T * top_k, E, offload_mask, rt);
+  permute_kernel<<<1, 1024, smem, st>>>(ids, T * top_k, E, offload_mask, skip_negative ? 1 : 0, rt);
 }
 
 }  // namespace moe

@@ -17,6 +17,14 @@ One step of a layer on rank r (``EpMoeLayer.forward``):
 5. all-to-all of the fp32 output rows back, in the order they came;
 6. ``moe_ep_combine``: weighted sum per token into bf16.
 
+With a ``PeerExchange`` (``moe_ep_peer_*``) the same step runs without a
+collective and without a host read: every rank publishes its token rows and
+their expert slots in its own device region; each owner's kernels read every
+rank's rows through CUDA IPC mappings, run the pairs it owns and store each
+fp32 output row straight into the token's rank's region; the token's rank
+then combines from its region.  Ranks hand over with epoch flags in the
+regions (bounded waits).
+
 Expert placement (``plan_placement``) balances expected load: experts sorted
 by routing frequency, each given to the least-loaded rank that still has a
 free slot, so a Zipf-skewed router does not pile its popular experts on one
@@ -163,6 +171,92 @@ class LoopbackComm:
         out.copy_(inp)
 
 
+class PeerExchange:
+    """One rank's side of a peer-memory exchange group (``moe_ep_group_*``).
+
+    The rank's region (its published token rows and slots, and the fp32
+    expert outputs the other ranks store for its tokens) is mapped into every
+    other rank's process through CUDA IPC (``connect_ipc``), or, for ranks
+    emulated in one process on one device, handed over directly
+    (``connect_emulated``).  One group serves every expert-parallel layer of
+    the rank that runs on the same stream: a step completes all of its
+    exchanges before the next one publishes.  ``max_tokens`` bounds the tokens
+    any rank publishes per step.
+    """
+
+    def __init__(self, rank: int, world: int, *, max_tokens: int, top_k: int, hidden: int, num_experts: int,
+                 device=None):
+        self.rank, self.world = int(rank), int(world)
+        self.max_tokens, self.top_k, self.hidden = int(max_tokens), int(top_k), int(hidden)
+        self.num_experts = int(num_experts)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        g = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(1024)
+        with torch.cuda.device(self.device):
+            rc = _lib.lib().moe_ep_group_create(self.rank, self.world, self.max_tokens, self.top_k, self.hidden,
+                                                self.num_experts, ctypes.byref(g), err, len(err))
+        if rc != _lib.MOE_OK:
+            raise _lib.MoeError(rc, err.value.decode())
+        self._g = g
+
+    @property
+    def handle(self):
+        return self._g
+
+    def ipc_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(_lib.EP_IPC_HANDLE_BYTES)
+        _lib.check_group(_lib.lib().moe_ep_group_ipc_handle(self._g, buf), self._g, "moe_ep_group_ipc_handle")
+        return buf.raw
+
+    def region_ptr(self) -> int:
+        p = ctypes.c_void_p()
+        _lib.check_group(_lib.lib().moe_ep_group_region(self._g, ctypes.byref(p)), self._g, "moe_ep_group_region")
+        return int(p.value)
+
+    def connect_ipc(self, group=None) -> None:
+        """Exchange IPC handles over a torch.distributed group and map every
+        other rank's region (collective: every rank calls it)."""
+        import torch.distributed as dist
+
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.ipc_handle(), group=group)
+        with torch.cuda.device(self.device):
+            for peer, h in enumerate(handles):
+                if peer != self.rank:
+                    _lib.check_group(_lib.lib().moe_ep_group_open_peer(self._g, peer, h), self._g,
+                                     "moe_ep_group_open_peer")
+
+    @staticmethod
+    def connect_emulated(groups: Sequence["PeerExchange"]) -> None:
+        """Ranks emulated in one process: every group sees every other's region."""
+        ptrs = [g.region_ptr() for g in groups]
+        for g in groups:
+            for peer, p in enumerate(ptrs):
+                if peer != g.rank:
+                    _lib.check_group(_lib.lib().moe_ep_group_set_peer(g._g, peer, p), g._g, "moe_ep_group_set_peer")
+
+    def read_status(self, stream=None) -> int:
+        st = ctypes.c_int32(0)
+        _lib.check_group(_lib.lib().moe_ep_group_read_status(self._g, ctypes.byref(st), _stream_handle(stream)),
+                         self._g, "moe_ep_group_read_status")
+        return int(st.value)
+
+    def close(self, barrier=None) -> None:
+        """Release the group.  ``barrier`` (e.g. torch.distributed.barrier) is
+        called after this rank's work has drained and again after it unmapped
+        the other regions, so no rank frees a region another still maps."""
+        if getattr(self, "_g", None) is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if barrier is not None:
+            barrier()
+        _lib.lib().moe_ep_group_close_peers(self._g)
+        if barrier is not None:
+            barrier()
+        _lib.lib().moe_ep_group_destroy(self._g)
+        self._g = None
+
+
 class EpStep:
     """The rank-side sequence of one expert-parallel step, independent of how
     the device steps are carried out (``EpMoeLayer`` binds them to the CUDA
@@ -186,9 +280,13 @@ class EpStep:
         st.recv_splits = theirs.sum(axis=1).tolist()
         st.recv_counts = theirs
 
-    def forward(self, x: torch.Tensor, logits: torch.Tensor, comm, out: Optional[torch.Tensor] = None):
+    def forward(self, x: torch.Tensor, logits: torch.Tensor, comm=None, out: Optional[torch.Tensor] = None,
+                tokens_per_rank: int = 0):
         """This rank's routed-expert output for its tokens x [T, H] bf16, with the
-        ids and weights it routed them to."""
+        ids and weights it routed them to.  Layers built with a peer exchange
+        ignore ``comm`` and take ``tokens_per_rank`` (see ``peer_experts``)."""
+        if getattr(self, "exchange", None) is not None:
+            return self.forward_peer(x, logits, out, tokens_per_rank=tokens_per_rank)
         ids, w = self.route(logits)
         st = self.dispatch(x, ids, w)
         recv_counts = torch.empty_like(st.slot_counts)
@@ -214,7 +312,8 @@ class EpMoeLayer(EpStep):
 
     def __init__(self, local_weights: LayerWeights, *, num_experts: int, top_k: int, slot_of_expert,
                  rank: int, world: int, router_use_softmax: bool = True, normalize_topk_prob: bool = True,
-                 max_tokens: int = 4096, max_rows: Optional[int] = None):
+                 max_tokens: int = 4096, max_rows: Optional[int] = None,
+                 exchange: Optional[PeerExchange] = None):
         if local_weights.shared is not None:
             raise ValueError("expert parallelism covers routed experts only (no shared expert)")
         self.num_experts, self.top_k = int(num_experts), int(top_k)
@@ -235,9 +334,23 @@ class EpMoeLayer(EpStep):
         self.router = _LayerHandle(self.num_experts, self.top_k, self.hidden, local_weights.inter_size,
                                    local_weights.bits, local_weights.group_size, router_use_softmax,
                                    normalize_topk_prob, self.max_tokens, self.device)
-        # rows through the local experts: top_k 1, one row per received pair
-        self.experts = MoeLayer(local_weights, top_k=1, router_use_softmax=router_use_softmax,
-                                normalize_topk_prob=normalize_topk_prob, max_tokens=self.max_rows)
+        self.exchange = exchange
+        if exchange is None:
+            # rows through the local experts: top_k 1, one row per received pair
+            self.experts = MoeLayer(local_weights, top_k=1, router_use_softmax=router_use_softmax,
+                                    normalize_topk_prob=normalize_topk_prob, max_tokens=self.max_rows)
+        else:
+            if (exchange.rank, exchange.world, exchange.num_experts, exchange.top_k, exchange.hidden) != \
+                    (self.rank, self.world, self.num_experts, self.top_k, self.hidden):
+                raise ValueError("the peer exchange group was made for another rank, world or layer shape")
+            if exchange.max_tokens < self.max_tokens:
+                raise ValueError("the peer exchange group's max_tokens is below the layer's")
+            if self.top_k > self.epr:
+                raise ValueError("the peer exchange needs top_k <= experts per rank")
+            # every rank's tokens through the local experts: pairs owned elsewhere are skipped
+            self.experts = MoeLayer(local_weights, top_k=self.top_k, router_use_softmax=router_use_softmax,
+                                    normalize_topk_prob=normalize_topk_prob,
+                                    max_tokens=self.world * exchange.max_tokens)
         self._send_local = torch.empty(self.max_tokens * self.top_k, dtype=torch.int64, device=self.device)
         self._local_ids = torch.arange(self.epr, dtype=torch.int64, device=self.device).repeat(self.world)
 
@@ -305,6 +418,58 @@ class EpMoeLayer(EpStep):
                                                  st.ret_rows.data_ptr(), out.data_ptr(), _stream_handle(stream)),
                        self.router._h, "moe_ep_combine")
         return out
+
+    # -- the peer-memory step (exchange given) ----------------------------------
+    def peer_publish(self, x: torch.Tensor, ids: torch.Tensor, stream=None) -> None:
+        """Phase 1: this rank's tokens and their expert slots into its region."""
+        if self.exchange is None:
+            raise RuntimeError("this layer was built without a peer exchange")
+        t = int(x.shape[0]) if x.dim() == 2 else -1
+        if t < 0:
+            raise ValueError("activations must be [T, H]")
+        if t > self.exchange.max_tokens:
+            raise ValueError(f"{t} tokens above the exchange's max_tokens {self.exchange.max_tokens}")
+        self._check(x, "activations", (t, self.hidden), torch.bfloat16)
+        self._check(ids, "topk_ids", (t, self.top_k), torch.int64)
+        g = self.exchange.handle
+        _lib.check_group(_lib.lib().moe_ep_peer_publish(g, x.contiguous().data_ptr(), ids.contiguous().data_ptr(), t,
+                                                        self.slot_of_expert.data_ptr(), _stream_handle(stream)),
+                         g, "moe_ep_peer_publish")
+
+    def peer_experts(self, pairs_hint: int, tokens_per_rank: int = 0, stream=None) -> None:
+        """Phase 2: every rank's pairs owned here through the local experts, the
+        outputs stored into their token's rank's region.  ``tokens_per_rank``
+        (0: the exchange's max_tokens) bounds every rank's tokens in this step;
+        ``pairs_hint`` only picks the kernels."""
+        g = self.exchange.handle
+        _lib.check_group(_lib.lib().moe_ep_peer_experts(g, self.experts.handle, int(tokens_per_rank),
+                                                        int(pairs_hint), _stream_handle(stream)),
+                         g, "moe_ep_peer_experts")
+
+    def peer_combine(self, ids: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     stream=None) -> torch.Tensor:
+        """Phase 3: the weighted combine of this rank's tokens from its region."""
+        t = int(ids.shape[0])
+        self._check(w, "topk_weights", (t, self.top_k), torch.bfloat16)
+        if out is not None:
+            self._check(out, "out", (t, self.hidden), torch.bfloat16)
+            if not out.is_contiguous():
+                raise ValueError("out must be contiguous")
+        out = out if out is not None else torch.empty(t, self.hidden, dtype=torch.bfloat16, device=self.device)
+        g = self.exchange.handle
+        _lib.check_group(_lib.lib().moe_ep_peer_combine(g, ids.contiguous().data_ptr(), w.contiguous().data_ptr(), t,
+                                                        out.data_ptr(), _stream_handle(stream)),
+                         g, "moe_ep_peer_combine")
+        return out
+
+    def forward_peer(self, x: torch.Tensor, logits: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None,
+                     tokens_per_rank: int = 0):
+        """One step over the peer exchange: no host synchronisation, no
+        collective.  ``tokens_per_rank`` as in ``peer_experts``."""
+        ids, w = self.route(logits, stream)
+        self.peer_publish(x, ids, stream)
+        self.peer_experts(int(x.shape[0]) * self.top_k, tokens_per_rank, stream)
+        return self.peer_combine(ids, w, out, stream), ids, w
 
     def set_gemm(self, mode: int) -> None:
         """Kernel selection of the local expert rows (see MoeLayer.set_gemm)."""

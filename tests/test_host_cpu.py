@@ -61,6 +61,35 @@ def test_null_handle_calls_fail_cleanly(lib):
     lib.moe_destroy(None)
 
 
+@pytest.mark.parametrize("args,needle", [
+    ((0, 0, 64, 8, 2048, 128), "world"),
+    ((0, 9, 64, 8, 2048, 128), "world"),
+    ((2, 2, 64, 8, 2048, 128), "rank"),
+    ((0, 2, 0, 8, 2048, 128), "max_tokens"),
+    ((0, 2, 64, 0, 2048, 128), "top_k"),
+    ((0, 2, 64, 8, 2044, 128), "hidden_size"),
+    ((0, 3, 64, 8, 2048, 128), "num_experts"),
+    ((0, 2, 64, 8, 2048, 4), "num_experts"),
+])
+def test_peer_group_rejects_bad_shapes_without_gpu(lib, args, needle):
+    from nano_ktrans_b200 import _lib
+
+    g = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(256)
+    assert lib.moe_ep_group_create(*args, ctypes.byref(g), err, len(err)) == _lib.MOE_EINVAL
+    assert needle in err.value.decode()
+    assert not g.value
+
+
+def test_peer_group_null_calls_fail_cleanly(lib):
+    from nano_ktrans_b200 import _lib
+
+    assert lib.moe_ep_peer_publish(None, None, None, 0, None, None) == _lib.MOE_EINVAL
+    assert lib.moe_ep_peer_experts(None, None, 0, 0, None) == _lib.MOE_EINVAL
+    assert lib.moe_ep_peer_combine(None, None, None, 0, None, None) == _lib.MOE_EINVAL
+    assert lib.moe_ep_group_destroy(None) == _lib.MOE_EINVAL
+
+
 @pytest.mark.parametrize("bits,group", [(4, 128), (4, 64), (8, 0), (8, 128)])
 def test_torch_quantizer_matches_oracle(bits, group):
     from nano_ktrans_b200.weights import quantize_symmetric
