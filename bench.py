@@ -189,14 +189,14 @@ def clone_layer(lw):
                         up_q=lw.up_q.clone(), up_s=lw.up_s.clone(), down_q=lw.down_q.clone(), down_s=lw.down_s.clone())
 
 
-def make_inputs(gen, n_layers, batch, device):
+def make_inputs(gen, n_layers, batch, device, with_router=False):
     import torch
 
     H, E = CFG["hidden"], CFG["experts"]
     x = torch.randn(n_layers, batch, H, generator=gen, device=device).to(torch.bfloat16)
     wr = (torch.randn(n_layers, E, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
     logits = torch.bmm(x, wr.transpose(1, 2))  # bf16 GEMM, as nn.Linear in bf16 computes the router
-    return x, logits.contiguous()
+    return (x, logits.contiguous(), wr) if with_router else (x, logits.contiguous())
 
 
 def expert_proj_bytes(lw):
@@ -272,6 +272,49 @@ def run_device(layers, x, logits, outs, steps, warmup, profile_layer_class=None)
         del g_prof
     del g_full, g_rem
     return ms, kern, launches
+
+
+def run_router_step(layers, x, wr, outs, steps, warmup):
+    """The decode step from hidden states (MoeLayer.forward_x: the router
+    projection kernel, then the single-launch step), captured for the L-layer
+    cycle in a CUDA graph and replayed like run_device.  Returns (ms for
+    `steps` steps, launches per step)."""
+    import torch
+
+    L = len(layers)
+    for i in range(warmup):
+        layers[i % L].forward_x(x[i % L], wr[i % L], out=outs[i % L])
+    torch.cuda.synchronize()
+    launches = layers[0].last_launch_count()
+    full, rem = divmod(steps, L)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
+                layers[i].forward_x(x[i], wr[i], out=outs[i])
+        return g
+
+    g_full = capture(L)
+    g_rem = capture(rem) if rem else None
+    g_full.replay()
+    torch.cuda.synchronize()
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(full):
+        g_full.replay()
+    if g_rem is not None:
+        g_rem.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    del g_full, g_rem
+    return e0.elapsed_time(e1), launches
 
 
 def distinct_experts(layers, logits):
@@ -602,7 +645,7 @@ def main():
     max_b = max([args.batch] + [int(b) for b in args.sweep.split(",") if b])
     layers = [MoeLayer(lw, top_k=CFG["top_k"], router_use_softmax=True, normalize_topk_prob=True, max_tokens=max_b)
               for lw in lws]
-    x, logits = make_inputs(gen, args.layers, args.batch, dev)
+    x, logits, wr = make_inputs(gen, args.layers, args.batch, dev, with_router=True)
     outs = torch.empty_like(x)
     gu_bytes, dn_bytes = expert_proj_bytes(lws[0])
     peak, peak_kind = hbm_peak()
@@ -653,6 +696,20 @@ def main():
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }
+
+    if fused:
+        # the same step from hidden states: the router projection (bf16 [E, H] per
+        # layer) runs in the timed graph too
+        r_ms, r_launch = run_router_step(layers, x, wr, outs, args.steps, args.warmup)
+        r_ms = max_over_ranks(r_ms)
+        router_bytes = CFG["experts"] * CFG["hidden"] * 2
+        r_step = r_ms / args.steps
+        line["decode_with_router"] = {
+            "value": args.steps * args.batch * world / (r_ms / 1e3), "unit": "tokens/s", "ms_per_step": r_step,
+            "launches_per_step": r_launch,
+            "bytes_per_step": statistics.mean(steps_bytes) + router_bytes, "router_bytes_per_step": router_bytes,
+            "frac_of_peak": (statistics.mean(steps_bytes) + router_bytes) / (r_step / 1e3) / 1e9 / peak,
+            "api": "MoeLayer.forward_x (moe_forward_x: router projection kernel + the single-launch step)"}
 
     if not args.no_c1 and args.batch == 1:
         line["c1_w8_decode_b1"] = run_c1(gen, dev, 48 * 500, 48,
