@@ -57,20 +57,29 @@ void launch_route(const uint16_t* logits, int T, int E, int top_k, bool use_soft
 // bf16, fp32 accumulation, one bf16 rounding).
 //
 // Warp-level tensor-core GEMM: a CTA owns 16 tokens x 8 experts (one
-// m16n8k16 output tile, tokens = M, experts = N) and its 8 warps split K in
-// 32-wide blocks (block b to warp b % 8); the 8 partial tiles are added in
+// m16n8k16 output tile, tokens = M, experts = N) and its 16 warps split K in
+// 32-wide blocks (block b to warp b % 16); the 16 partial tiles are added in
 // warp order in shared memory.  Lane (g, t) takes the 8 consecutive k of
 // block b starting at 8t, from token rows g and g + 8 (A) and expert row g
 // (B); the two mma steps of the block use pairs (0,1),(2,3) and (4,5),(6,7) of
 // those 8 values, the same permutation of K on both operands.
+//
+// Latency: a warp's first kRouterPrefetch blocks of Wr are loaded before the
+// programmatic-dependency wait (the router weights are not written by the
+// kernel this launch may overlap: only this library's kernels trigger an early
+// launch, and none of them writes router weights), so their DRAM round trip
+// overlaps the previous kernel's tail; x, which the previous kernel may have
+// written, is read after the wait, all of a warp's blocks at once.
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
-                                                            const uint16_t* __restrict__ wr, int T, int E, int H,
-                                                            uint16_t* __restrict__ logits) {
-  __shared__ float part[8][16][9];
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+constexpr int kRouterWarps = 16;
+constexpr int kRouterPrefetch = 4;  // blocks per warp per round: H <= 16 * 4 * 32 = 2048 in one round
+
+__global__ void __launch_bounds__(kRouterWarps * 32) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                                         const uint16_t* __restrict__ wr, int T,
+                                                                         int E, int H,
+                                                                         uint16_t* __restrict__ logits) {
+  __shared__ float part[kRouterWarps][16][9];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int tok0 = blockIdx.y * 16, e0 = blockIdx.x * 8;
@@ -78,22 +87,40 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
   const uint16_t* xa = x + static_cast<size_t>(ok_a ? tok0 + g : 0) * H + 8 * t;
   const uint16_t* xb = x + static_cast<size_t>(ok_b ? tok0 + g + 8 : 0) * H + 8 * t;
   const uint16_t* wp = wr + static_cast<size_t>(ok_w ? e0 + g : 0) * H + 8 * t;
-  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
   const int nb = H / 32;
-#pragma unroll 4
-  for (int b = warp; b < nb; b += 8) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    const uint4 va = ok_a ? *reinterpret_cast<const uint4*>(xa + 32 * b) : z;
-    const uint4 vb = ok_b ? *reinterpret_cast<const uint4*>(xb + 32 * b) : z;
-    const uint4 vw = ok_w ? *reinterpret_cast<const uint4*>(wp + 32 * b) : z;
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c0[0]), "+f"(c0[1]), "+f"(c0[2]), "+f"(c0[3])
-        : "r"(va.x), "r"(vb.x), "r"(va.y), "r"(vb.y), "r"(vw.x), "r"(vw.y));
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c1[0]), "+f"(c1[1]), "+f"(c1[2]), "+f"(c1[3])
-        : "r"(va.z), "r"(vb.z), "r"(va.w), "r"(vb.w), "r"(vw.z), "r"(vw.w));
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  uint4 pre[kRouterPrefetch];
+#pragma unroll
+  for (int i = 0; i < kRouterPrefetch; ++i) {
+    const int b = warp + i * kRouterWarps;
+    pre[i] = ok_w && b < nb ? *reinterpret_cast<const uint4*>(wp + 32 * b) : z;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int r = 0; r * kRouterWarps * kRouterPrefetch < nb; ++r) {
+    uint4 va[kRouterPrefetch], vb[kRouterPrefetch];
+#pragma unroll
+    for (int i = 0; i < kRouterPrefetch; ++i) {
+      const int b = warp + (r * kRouterPrefetch + i) * kRouterWarps;
+      const bool in = b < nb;
+      va[i] = ok_a && in ? *reinterpret_cast<const uint4*>(xa + 32 * b) : z;
+      vb[i] = ok_b && in ? *reinterpret_cast<const uint4*>(xb + 32 * b) : z;
+      if (r > 0) pre[i] = ok_w && in ? *reinterpret_cast<const uint4*>(wp + 32 * b) : z;
+    }
+    uint4* vw = pre;
+#pragma unroll
+    for (int i = 0; i < kRouterPrefetch; ++i) {
+      if (warp + (r * kRouterPrefetch + i) * kRouterWarps >= nb) break;  // warp-uniform
+      asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+          "{%0,%1,%2,%3};"
+          : "+f"(c0[0]), "+f"(c0[1]), "+f"(c0[2]), "+f"(c0[3])
+          : "r"(va[i].x), "r"(vb[i].x), "r"(va[i].y), "r"(vb[i].y), "r"(vw[i].x), "r"(vw[i].y));
+      asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+          "{%0,%1,%2,%3};"
+          : "+f"(c1[0]), "+f"(c1[1]), "+f"(c1[2]), "+f"(c1[3])
+          : "r"(va[i].z), "r"(vb[i].z), "r"(va[i].w), "r"(vb[i].w), "r"(vw[i].z), "r"(vw[i].w));
+    }
   }
   // c[0] = (token g, expert 2t), c[1] = (g, 2t+1), c[2] = (g+8, 2t), c[3] = (g+8, 2t+1)
   part[warp][g][2 * t] = c0[0] + c1[0];
@@ -105,7 +132,7 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
     const int r = threadIdx.x >> 3, c = threadIdx.x & 7;
     float v = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) v += part[w][r][c];
+    for (int w = 0; w < kRouterWarps; ++w) v += part[w][r][c];
     if (tok0 + r < T && e0 + c < E) logits[static_cast<size_t>(tok0 + r) * E + e0 + c] = f32_to_bf16(v);
   }
 }
@@ -120,7 +147,7 @@ void launch_router_logits(const uint16_t* x, const uint16_t* wr, int T, int E, i
   if (T <= 0) return;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((E + 7) / 8, (T + 15) / 16);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kRouterWarps * 32);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
