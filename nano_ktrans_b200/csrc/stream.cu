@@ -76,6 +76,8 @@ template <bool GATEUP> struct Roles {
 constexpr int kTok = 8;  // tokens per chunk: the mma's N
 constexpr int kMaxStages = 8;
 constexpr int kRedBufs = 3;
+// largest K-part count: gate/up always 8; down divides its 12 consumer warps
+template <bool GATEUP> struct PartsCap { static constexpr int value = GATEUP ? 8 : 12; };
 // A partial-sum buffer holds red[token][K-part][item row]: the epilogue's lanes
 // read consecutive rows of one part (no bank conflicts).  Item rows x P is at
 // most 256 (gate/up: 2R rows, R = 128 / P; down: R = 16 * consumers / P rows).
@@ -292,6 +294,7 @@ MOE_DEV void item_compute(const unsigned char* st, const uint16_t* sc, const uin
 
 template <bool GATEUP, int GPW>
 __global__ void __launch_bounds__(Roles<GATEUP>::kThreads, 1) stream_kernel(Args a) {
+  constexpr int kMaxParts = PartsCap<GATEUP>::value;
   constexpr int kConsumerWarps = Roles<GATEUP>::kConsumerWarps, kProducerWarp = Roles<GATEUP>::kProducerWarp,
                 kEpilogueWarp = Roles<GATEUP>::kEpilogueWarp, kEpilogueWarps = Roles<GATEUP>::kEpilogueWarps,
                 kThreads = Roles<GATEUP>::kThreads;
@@ -452,6 +455,8 @@ __global__ void __launch_bounds__(Roles<GATEUP>::kThreads, 1) stream_kernel(Args
         ac::bulk_g2s(ac::smem_u32(raw + static_cast<size_t>(lane) * rowsz), src, rowsz, bar(kBarRaw));
       }
     };
+    // lanes per token in an epilogue pass: R is 16 or a multiple of 32 ... (16 | R)
+    const int lsh = R < 32 ? 4 : 5, lpt = 1 << lsh, tpp = 32 / lpt;
     Cursor cur{tab, cap}, ahead{tab, cap};
     int gc = lo / blocks, rbk = lo - gc * blocks;
     const int gc_last = (hi - 1) / blocks;
@@ -475,26 +480,36 @@ __global__ void __launch_bounds__(Roles<GATEUP>::kThreads, 1) stream_kernel(Args
         stage_rows(ahead.at(gc + 1));
         ++staged;
       }
-      // outputs (token n, row r) of this item, n-major; this warp takes half
+      // outputs (token n, row r) of this item: a pass of the warp covers tpp
+      // tokens (lane >> lsh) and rows r = lane & (lpt - 1) (+ lpt ...); the
+      // warps take passes in turn.  All P partials of an output are loaded before
+      // they are added in part order (independent shared loads, one dependent
+      // add chain); consecutive lanes read consecutive rows (no bank conflicts).
       const float* rp = red + b * kRedFloats;
       float* ob = a.out + static_cast<size_t>(c.s0) * N + rbk * R;
       const int rows = GATEUP ? 2 * R : R;  // item rows in the partial-sum buffer
-      const int half = (R * kTok) / kEpilogueWarps;
-#pragma unroll 2
-      for (int o = ew * half + lane; o < (ew + 1) * half; o += 32) {
-        const int n = o / R, r = o - n * R;
+      for (int n0 = ew * tpp; n0 < kTok; n0 += kEpilogueWarps * tpp) {
+        const int n = n0 + (lane >> lsh);
         if (n >= c.cnt) continue;
-        // partials red[n][q][row] for q = 0..P-1, added in part order; consecutive
-        // lanes read consecutive rows (no bank conflicts)
-        const float* pg = rp + n * P * rows + r;
-        float gs = 0.0f, us = 0.0f;
-#pragma unroll 4
-        for (int q = 0; q < P; ++q) {
-          gs += pg[q * rows];
-          if constexpr (GATEUP) us += pg[q * rows + R];
+        for (int r = lane & (lpt - 1); r < R; r += lpt) {
+          const float* pg = rp + n * P * rows + r;
+          float pv[kMaxParts], pu[GATEUP ? kMaxParts : 1];
+#pragma unroll
+          for (int q = 0; q < kMaxParts; ++q) {
+            pv[q] = q < P ? pg[q * rows] : 0.0f;
+            if constexpr (GATEUP) pu[q] = q < P ? pg[q * rows + R] : 0.0f;
+          }
+          float gs = 0.0f, us = 0.0f;
+#pragma unroll
+          for (int q = 0; q < kMaxParts; ++q) {
+            if (q < P) {
+              gs += pv[q];
+              if constexpr (GATEUP) us += pu[q];
+            }
+          }
+          const float v = GATEUP ? silu_f32(gs) * us : gs;
+          ob[static_cast<size_t>(n) * N + r] = v;
         }
-        const float v = GATEUP ? silu_f32(gs) * us : gs;
-        ob[static_cast<size_t>(n) * N + r] = v;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kBarRedEmpty + b));
@@ -678,12 +693,12 @@ static bool plan(const QuantProj& p0, int max_active, Plan& pl) {
   if (K % 128 || p0.group % 128 || K % p0.group) return false;
   const int nG = K / 128;
   const int P = pick_parts<GATEUP>(nG, N);
-  if (P == 0) return false;
+  if (P == 0 || P > PartsCap<GATEUP>::value) return false;
   const int gpw = (nG + P - 1) / P;
   if (gpw > 2) return false;
   const int tiles = Roles<GATEUP>::kConsumerWarps / P;
   const int R = GATEUP ? 16 * tiles / 2 : 16 * tiles;
-  if (R < 16 || N % R) return false;
+  if (R < 16 || N % R || (R > 16 && R % 32)) return false;  // the epilogue's lane split: R = 16 or 32j
   const uint32_t rowb = static_cast<uint32_t>(K / 2);
   const uint32_t code = (GATEUP ? 2u : 1u) * R * rowb;
   const uint32_t scale = (GATEUP ? 2u : 1u) * R * p0.sstride * 2u;
