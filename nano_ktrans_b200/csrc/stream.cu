@@ -24,8 +24,8 @@
 // chunk-major, and each CTA of the persistent grid takes one contiguous range
 // of items, so a CTA sees one or two chunks and streams their rows in order.
 //
-// Warp roles, one CTA per SM (gate/up: C = 16 consumer warps, E = 2 epilogue
-// warps; down: C = 12, E = 4 — see Roles):
+// Warp roles, one CTA per SM (gate/up: C = 16 consumer warps, E = 3 epilogue
+// warps; down: C = 12, E = 7 — see Roles):
 //   warps 0..C-1  consumers.  P K-parts x (C / P) 16-row tiles: warp w
 //               computes tile w / P of the item over the 128-code groups p,
 //               p + P, ... of K-part p = w % P.  Gate/up tiles alternate gate
@@ -63,14 +63,16 @@
 namespace moe {
 namespace sm {
 
-// Warp roles per projection: gate/up 16 consumer warps, 1 producer, 2 epilogue
+// Warp roles per projection: gate/up 16 consumer warps, 1 producer, 3 epilogue
 // warps; down (whose items are small and whose every output sums P partials)
-// 12 consumer warps and 4 epilogue warps.
+// 12 consumer warps and 7 epilogue warps.  20 warps: at most 5 share an SM
+// sub-partition's 16K registers, which keeps 96 registers per thread (21 warps
+// would cap them at 80).
 template <bool GATEUP> struct Roles {
   static constexpr int kConsumerWarps = GATEUP ? 16 : 12;
   static constexpr int kProducerWarp = kConsumerWarps;
   static constexpr int kEpilogueWarp = kConsumerWarps + 1;
-  static constexpr int kEpilogueWarps = GATEUP ? 2 : 4;
+  static constexpr int kEpilogueWarps = GATEUP ? 3 : 7;
   static constexpr int kThreads = (kEpilogueWarp + kEpilogueWarps) * 32;
 };
 constexpr int kTok = 8;  // tokens per chunk: the mma's N
