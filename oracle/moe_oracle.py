@@ -26,7 +26,7 @@ golden vectors produced by running the reference itself
 (``tests/golden/make_golden.py`` drives the reference ``HybridMoE.forward`` ->
 ``CPUMoEBackend`` GPTQ path live and records its outputs).
 
-Scale convention (the survey's rule for "bf16 scales"): scales and codes are
+Scale convention for bf16 scales: scales and codes are
 computed in fp32 exactly as the reference quantizer does, then the stored
 scales are rounded to bf16; every consumer dequantizes with the bf16-valued
 scale, which makes ``(q - z) * s`` exact in fp32.
