@@ -1349,7 +1349,80 @@ def run_ep(args, world, rank, dev, uniq, lws):
     if exchange is not None:
         exchange.close(barrier=torch.distributed.barrier)
     torch.cuda.empty_cache()
+    if world > 1:
+        # the N = 1 configuration measured in the same run: every rank puts the
+        # whole global batch through the single-GPU path on its own GPU (local
+        # work; then every rank takes the same collective steps)
+        one = single_gpu_same_run(args, lws, routers, biases, n_prefill, n_decode, dev)
+        ok = torch.tensor([1.0 if one is not None else 0.0], device=dev)
+        torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+        p1 = max_over_ranks(one[0] if one is not None else 0.0)
+        d1 = max_over_ranks(one[1] if one is not None else 0.0)
+        if float(ok.item()) == 1.0:
+            res["single_gpu_same_run"] = {
+                "prefill_ms_per_48_layers": p1, "decode_ms_per_48_layers": d1,
+                "path": "moe_forward per layer, all experts on one GPU, the global batches, max over ranks"}
+            res["prefill"]["scaling_efficiency"] = p1 / (world * res["prefill"]["ms_per_48_layers"])
+            res["decode"]["scaling_efficiency"] = d1 / (world * res["decode"]["ms_per_48_layers"])
     return res
+
+
+def single_gpu_same_run(args, lws, routers, biases, n_prefill, n_decode, dev):
+    """The global prefill and decode batches through the single-GPU path
+    (MoeLayer.forward per layer, every expert local) on this rank's GPU, timed
+    like the expert-parallel passes (a CUDA graph of the 48-layer pass when
+    --ep-graph).  Local work only.  Returns (prefill ms, decode ms) per pass,
+    or None when it could not run (the reason goes to stderr)."""
+    import torch
+
+    from nano_ktrans_b200.moe_layer import MoeLayer
+
+    k, H = CFG["top_k"], CFG["hidden"]
+    layers1 = []
+    try:
+        gen = torch.Generator(device=dev).manual_seed(args.seed + 7000)  # the same batches on every rank
+
+        def gbatch(n):
+            xs = [torch.randn(n, H, generator=gen, device=dev).to(torch.bfloat16) for _ in range(len(lws))]
+            lg = [((x @ r.T).float() + b).to(torch.bfloat16) for x, r, b in zip(xs, routers, biases)]
+            return xs, lg
+
+        xp1, lp1 = gbatch(n_prefill)
+        xd1, ld1 = gbatch(n_decode)
+        layers1 = [MoeLayer(lw, top_k=k, router_use_softmax=True, normalize_topk_prob=True, max_tokens=n_prefill)
+                   for lw in lws]
+
+        def time_pass(xs, lg, steps):
+            def step():
+                for lay, x, g in zip(layers1, xs, lg):
+                    lay.forward(x, g)
+            step()
+            torch.cuda.synchronize()
+            run, graph = step, None
+            if args.ep_graph:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    step()
+                run = graph.replay
+                run()
+                torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                run()
+            e1.record()
+            torch.cuda.synchronize()
+            del graph
+            return e0.elapsed_time(e1) / steps
+
+        return time_pass(xp1, lp1, args.ep_steps), time_pass(xd1, ld1, 3 * args.ep_steps)
+    except Exception as exc:  # reported, and the efficiency keys are left out on every rank
+        print(f"single-GPU reference pass not run: {exc}", file=sys.stderr, flush=True)
+        return None
+    finally:
+        for lay in layers1:
+            lay.close()
+        torch.cuda.empty_cache()
 
 
 def ep_cpu_baseline(layer, lw, xp, lp, xd, ld, n_layers, seconds):
