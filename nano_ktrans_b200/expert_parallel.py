@@ -441,6 +441,8 @@ class EpMoeLayer(EpStep):
         outputs stored into their token's rank's region.  ``tokens_per_rank``
         (0: the exchange's max_tokens) bounds every rank's tokens in this step;
         ``pairs_hint`` only picks the kernels."""
+        if self.exchange is None:
+            raise RuntimeError("this layer was built without a peer exchange")
         g = self.exchange.handle
         _lib.check_group(_lib.lib().moe_ep_peer_experts(g, self.experts.handle, int(tokens_per_rank),
                                                         int(pairs_hint), _stream_handle(stream)),
@@ -449,7 +451,12 @@ class EpMoeLayer(EpStep):
     def peer_combine(self, ids: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
                      stream=None) -> torch.Tensor:
         """Phase 3: the weighted combine of this rank's tokens from its region."""
+        if self.exchange is None:
+            raise RuntimeError("this layer was built without a peer exchange")
+        if ids.dim() != 2:
+            raise ValueError("topk_ids must be [T, top_k]")
         t = int(ids.shape[0])
+        self._check(ids, "topk_ids", (t, self.top_k), torch.int64)
         self._check(w, "topk_weights", (t, self.top_k), torch.bfloat16)
         if out is not None:
             self._check(out, "out", (t, self.hidden), torch.bfloat16)
