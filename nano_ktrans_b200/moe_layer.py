@@ -173,11 +173,19 @@ class MoeLayer:
         """forward() on host tensors (bf16, contiguous, ideally pinned): copies in,
         runs the step and copies the result into `out`, all enqueued on the
         stream — `out` is valid after the stream is synchronised."""
-        for name, tsr, cols in (("x", x, self.hidden_size), ("router_logits", router_logits, self.num_experts),
-                                ("out", out, self.hidden_size)):
-            if (tsr.device.type != "cpu" or tsr.dtype is not torch.bfloat16 or tsr.dim() != 2
-                    or tsr.shape[1] != cols or tsr.shape[0] != x.shape[0] or not tsr.is_contiguous()):
-                raise ValueError(f"{name} must be a contiguous bf16 host tensor [T, {cols}]")
+        # one combined test on the per-step path (a few attribute reads per tensor);
+        # the per-tensor loop below only names the offending argument
+        bf, t = torch.bfloat16, x.shape[0] if x.dim() == 2 else -1
+        if not (x.is_cpu and router_logits.is_cpu and out.is_cpu and x.dtype is bf and router_logits.dtype is bf
+                and out.dtype is bf and x.shape == (t, self.hidden_size)
+                and router_logits.shape == (t, self.num_experts) and out.shape == (t, self.hidden_size)
+                and x.is_contiguous() and router_logits.is_contiguous() and out.is_contiguous()):
+            for name, tsr, cols in (("x", x, self.hidden_size), ("router_logits", router_logits, self.num_experts),
+                                    ("out", out, self.hidden_size)):
+                if (tsr.device.type != "cpu" or tsr.dtype is not bf or tsr.dim() != 2
+                        or tsr.shape[1] != cols or tsr.shape[0] != t or not tsr.is_contiguous()):
+                    raise ValueError(f"{name} must be a contiguous bf16 host tensor [T, {cols}]")
+            raise ValueError("x, router_logits and out must be contiguous bf16 host tensors of T rows")
         _lib.check(_lib.lib().moe_forward_host(self._h, x.data_ptr(), router_logits.data_ptr(), int(x.shape[0]),
                                                out.data_ptr(), _stream_handle(stream)), self._h, "moe_forward_host")
 
